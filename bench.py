@@ -1,0 +1,381 @@
+"""Benchmark of the NVFP4 Gated DeltaNet decode step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU)
+
+Workload (one "step"): one decode token for each of 256 sequences through one
+GDN layer (16 key heads, 32 value heads, d_k = d_v = 128) whose NVFP4 state
+pool holds 256 slots (slot i -> sequence i), on every GPU.  Scaling is weak:
+each rank owns its own sequences and pool, with no collective on the data path
+(only a barrier and a max-reduction of the timings).
+
+Timing: W untimed warm-up steps, then exactly K steps bracketed by a barrier
+and torch.cuda.synchronize(), measured with CUDA events on the launching
+stream; the whole-job time is the max over ranks.  Inputs rotate over 6 pools
+and 6 input sets (453 MB, larger than the 126 MB L2), so every step reads its
+state from HBM.  Per-launch kernel durations come from events around each
+launch and give the roofline figure: achieved = 614,916 algorithmic bytes per
+token (NVFP4 state read + write, global scales, bf16 q/k/v/o, g/beta, slot
+index) x 256 tokens / mean launch duration.
+
+The e2e figure is the same metric through the public API with host buffers:
+per step, pinned-host -> device copies of that step's q, k, v, g, beta and slot
+indices, the decode call, and a device -> pinned-host copy of its outputs.
+
+rank 0 at N = 1 also times the CPU path (the reference's NVFP4 host codec from
+oracle/_ref around a C restatement of the GDN step, all host threads) on a
+bounded sample of the same workload.
+
+--impl reference: rank 0 times that CPU path alone on the same config and prints
+the same JSON line with "impl": "reference" (other ranks exit without work).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import pathlib
+import statistics
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+PKG = ROOT / "blackwell-kernel-sm_120_b200"
+for _p in (str(ROOT), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "GDN decode tokens/s (NVFP4 state, batch-256 decode step)"
+UNIT = "tokens/s"
+B, HK, HV, D = 256, 16, 32, 128
+NUM_SLOTS = 256
+N_POOLS = 6
+BYTES_PER_TOKEN = 614_916  # 32 x (8192 + 1024) x 2 + 32 x 4 x 2 + 24,576 + 256 + 4
+WORKLOAD = "decode_b256_hk16_hv32_d128_pool256"
+
+
+def _config(n_gpus: int) -> dict:
+    return {"workload": WORKLOAD, "batch_per_gpu": B, "num_k_heads": HK, "num_v_heads": HV, "head_dim": D,
+            "pool_slots": NUM_SLOTS, "state_format": "nvfp4 e2m1 + ue4m3/16 + fp32 per-head global scale",
+            "scale_mode": "ref240", "parallelism": f"dp{n_gpus} (sequences sharded, no collective)",
+            "l2": f"inputs rotate over {N_POOLS} pools + input sets (453 MB > 126 MB L2)"}
+
+
+# ---- clocks -----------------------------------------------------------------------------
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        "hw_slowdown": 0x0000000000000008, "sw_thermal_slowdown": 0x0000000000000020,
+        "hw_thermal_slowdown": 0x0000000000000040, "hw_power_brake_slowdown": 0x0000000000000080,
+        "sw_power_cap": 0x0000000000000004,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._period = period_s
+        self._ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._ok = True
+        except Exception:
+            self._nv = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _sample(self):
+        clk = self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM)
+        reasons = self._nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+        self.samples.append((clk, reasons))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._ok:
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._ok:
+            self._stop.set()
+            self._t.join()
+            if not self.samples:
+                self._sample()
+
+    def summary(self) -> dict:
+        if not self._ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        mask = 0
+        for _, r in self.samples:
+            mask |= r
+        reasons = [n for n, bit in self.REASONS.items() if mask & bit]
+        return {"sm_mhz": statistics.median(c for c, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ---- distributed plumbing --------------------------------------------------------------------
+
+def _dist_init(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        return dist, dist.get_rank(), world, local
+    return None, 0, 1, 0
+
+
+def _barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def _max_over_ranks(dist, x: float) -> float:
+    if dist is None:
+        return x
+    import torch
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---- CPU path ---------------------------------------------------------------------------------
+
+def cpu_decode_sample(seconds: float, threads: int | None = None) -> dict:
+    """Times the CPU decode step on a bounded sample of the workload: repeated
+    passes over `sample_seqs` sequences (all 32 heads each) until `seconds`."""
+    import numpy as np
+    from gdn_b200 import workloads
+    from oracle import bindings as ob
+
+    lib, kind = ob.cpu_baseline(prefer_reference=True)
+    nthreads = threads or lib.cpu_max_threads()
+    sample_seqs = 16
+    x = workloads.decode_steps(sample_seqs, 1, HK, HV, D, seed=0)
+    states = workloads.initial_states(sample_seqs, HV, D, seed=1).numpy()
+    codes, scales, gs, _ = ob.quantise_tiles(states.reshape(-1), D * D, 0)
+    codes = codes.reshape(sample_seqs, HV, D, D // 2).copy()
+    scales = scales.reshape(sample_seqs, HV, D, D // 16).copy()
+    gs = gs.reshape(sample_seqs, HV).copy()
+
+    def bits(t):
+        return np.ascontiguousarray(t.contiguous().view(__import__("torch").int16).numpy().view(np.uint16))
+
+    q, k, v = bits(x["q"][0]), bits(x["k"][0]), bits(x["v"][0])
+    g, be = np.ascontiguousarray(x["g"][0].numpy()), np.ascontiguousarray(x["beta"][0].numpy())
+    slot = np.arange(sample_seqs, dtype=np.int32)
+    o = np.zeros((sample_seqs, HV, D), np.uint16)
+    P = ob._ptr
+    calls = 0
+    t0 = time.perf_counter()
+    while True:
+        lib.cpu_gdn_decode(sample_seqs, HK, HV, D, P(q), P(k), P(v), P(g), P(be), P(slot), P(codes), P(scales),
+                           P(gs), P(o), 1.0 / math.sqrt(D), 0, 1440.0, 0, sample_seqs * HV, nthreads)
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": calls * sample_seqs / el, "unit": UNIT, "cores": nthreads, "kind": kind,
+            "sample": (f"{calls} passes x {sample_seqs} sequences x {HV} heads of the same decode step "
+                       f"({el:.1f} s); reference NVFP4 host codec (oracle/_ref) around a C restatement of the "
+                       f"GDN step" if kind == "reference" else "oracle port of the CPU path")}
+
+
+# ---- GPU path ---------------------------------------------------------------------------------------
+
+def _traffic_from_profile() -> float | None:
+    p = ROOT / "profiles" / "gdn_decode_b256_traffic.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["dram_bytes_per_launch"])
+        except Exception:
+            return None
+    return None
+
+
+def run_ours(args, dist, rank, world, local) -> dict | None:
+    import torch
+    from gdn_b200 import NVFP4StatePool, ops, workloads
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    # pools and inputs (seeded per rank: each rank owns distinct sequences)
+    pools, inputs = [], []
+    gen = torch.Generator(device=dev)
+    for i in range(N_POOLS):
+        gen.manual_seed(1000 * rank + i)
+        p = NVFP4StatePool.zeros(NUM_SLOTS, HV, D, dev)
+        st = torch.randn((NUM_SLOTS, HV, D, D), generator=gen, device=dev) * 0.02
+        p.load_fp32(st)
+        del st
+        pools.append(p)
+        inputs.append({k2: t[0] for k2, t in workloads.decode_steps(B, 1, HK, HV, D, seed=100 * rank + i,
+                                                                     device=dev).items()})
+    slot = torch.arange(B, dtype=torch.int32, device=dev)
+    out = torch.empty((B, HV, D), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        x = inputs[i % N_POOLS]
+        ops.decode(x["q"], x["k"], x["v"], x["g"], x["beta"], slot, pools[i % N_POOLS], out=out)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if ops.device_status(clear=True):
+        raise RuntimeError("device status set during warm-up")
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    t_begin = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    _barrier(dist)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        t_begin.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            step(args.warmup + i)
+            ends[i].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    _barrier(dist)
+    total_ms = t_begin.elapsed_time(t_end)
+    launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = _max_over_ranks(dist, total_ms)
+    mean_launch_ms = _max_over_ranks(dist, sum(launch_ms) / len(launch_ms))
+    if ops.device_status(clear=True):
+        raise RuntimeError("device status set during the timed region")
+
+    # e2e: through the public API with pinned host buffers
+    host_in = []
+    for i in range(N_POOLS):
+        x = inputs[i]
+        host_in.append({k2: t.cpu().pin_memory() for k2, t in x.items()})
+    host_slot = slot.cpu().pin_memory()
+    dev_in = {k2: torch.empty_like(t) for k2, t in inputs[0].items()}
+    dev_slot = torch.empty_like(slot)
+    host_out = torch.empty((B, HV, D), dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host_in[0].values()) + host_slot.numel() * 4
+    d2h = host_out.numel() * 2
+    e2e_steps = max(1, min(args.steps, 200))
+
+    def e2e_step(i):
+        for k2 in dev_in:
+            dev_in[k2].copy_(host_in[i % N_POOLS][k2], non_blocking=True)
+        dev_slot.copy_(host_slot, non_blocking=True)
+        ops.decode(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], dev_slot,
+                   pools[i % N_POOLS], out=out)
+        host_out.copy_(out, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    _barrier(dist)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = _max_over_ranks(dist, e0.elapsed_time(e1))
+    _barrier(dist)
+
+    if rank != 0:
+        return None
+    tokens = B * world * args.steps
+    value = tokens / (total_ms / 1e3)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs")
+    peak_note = "measured" if peak else "fallback"
+    peak = peak or 6650.0
+    achieved = BYTES_PER_TOKEN * B / (mean_launch_ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 math, nvfp4 state, bf16 io", "data": "synthetic",
+        "config": _config(world),
+        "e2e": {"value": round(B * world * e2e_steps / (e2e_ms / 1e3), 1), "unit": UNIT,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": _traffic_from_profile(),
+                     "peak_source": peak_note, "kernel": "gdn_decode_kernel",
+                     "mean_launch_us": round(mean_launch_ms * 1e3, 3)},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_decode_sample(args.cpu_seconds)
+    return line
+
+
+def run_reference(args, rank) -> dict | None:
+    if rank != 0:
+        return None
+    per_step = []
+    info = None
+    for _ in range(args.warmup):
+        cpu_decode_sample(0.0)
+    for _ in range(args.steps):
+        info = cpu_decode_sample(0.0)
+        per_step.append(info["value"])
+    # value: tokens/s over the timed steps (each step one bounded pass)
+    value = statistics.mean(per_step)
+    cb = {"value": round(value, 2), "unit": UNIT, "cores": info["cores"], "kind": info["kind"],
+          "sample": "each step: one pass of 16 sequences x 32 heads of the decode step; " + info["sample"]}
+    return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(16 / value * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32 math, nvfp4 state, bf16 io", "data": "synthetic",
+            "config": _config(args.gpus), "impl": "reference", "cpu_baseline": cb,
+            "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "gpu_launches": 0}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        line = run_reference(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    dist, rank, world, local = _dist_init(args.gpus)
+    try:
+        line = run_ours(args, dist, rank, world, local)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

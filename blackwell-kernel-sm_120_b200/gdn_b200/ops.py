@@ -1,0 +1,202 @@
+"""Torch-tensor front end of the C ABI (include/gdn_b200.h).
+
+Each function validates shapes and dtypes, then calls the library on the
+current CUDA stream of the tensors' device.  Outputs are allocated by the
+caller or here with torch (never by the library).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _capi
+from ._capi import SCALE_FN448, SCALE_REF240, check, lib
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+# ---- NVFP4 codec --------------------------------------------------------------
+
+def nvfp4_quantize(x: torch.Tensor, scale_mode: int = SCALE_REF240) -> tuple[torch.Tensor, torch.Tensor]:
+    """Reference quantiser on the GPU: x (fp32, numel % 16 == 0) -> (codes, scales)."""
+    _need(x, torch.float32, "x")
+    n = x.numel()
+    codes = torch.empty(n // 2, dtype=torch.uint8, device=x.device)
+    scales = torch.empty(n // 16, dtype=torch.uint8, device=x.device)
+    check("gdn_nvfp4_quantize", lib.gdn_nvfp4_quantize(_ptr(x), _ptr(codes), _ptr(scales), n, scale_mode,
+                                                          _stream(x)))
+    return codes, scales
+
+
+def nvfp4_dequantize(codes: torch.Tensor, scales: torch.Tensor, scale_mode: int = SCALE_REF240) -> torch.Tensor:
+    _need(codes, torch.uint8, "codes")
+    _need(scales, torch.uint8, "scales")
+    n = codes.numel() * 2
+    if scales.numel() * 16 != n:
+        raise ValueError("scales must hold one byte per 16 elements")
+    out = torch.empty(n, dtype=torch.float32, device=codes.device)
+    check("gdn_nvfp4_dequantize", lib.gdn_nvfp4_dequantize(_ptr(codes), _ptr(scales), _ptr(out), n, scale_mode,
+                                                              _stream(codes)))
+    return out
+
+
+def nvfp4_quantize_tiles(x: torch.Tensor, tile_elems: int, scale_mode: int = SCALE_REF240,
+                         gscale_den: float = 0.0):
+    """Per-tile global scale + reference quantiser: returns (codes, scales, gscale)."""
+    _need(x, torch.float32, "x")
+    n = x.numel()
+    if tile_elems <= 0 or n % tile_elems or tile_elems % 16:
+        raise ValueError("numel must be a multiple of tile_elems, itself a multiple of 16")
+    nt = n // tile_elems
+    codes = torch.empty(n // 2, dtype=torch.uint8, device=x.device)
+    scales = torch.empty(n // 16, dtype=torch.uint8, device=x.device)
+    gs = torch.empty(nt, dtype=torch.float32, device=x.device)
+    check("gdn_nvfp4_quantize_tiles",
+          lib.gdn_nvfp4_quantize_tiles(_ptr(x), nt, tile_elems, _ptr(codes), _ptr(scales), _ptr(gs), scale_mode,
+                                       gscale_den, _stream(x)))
+    return codes, scales, gs
+
+
+def nvfp4_dequantize_tiles(codes: torch.Tensor, scales: torch.Tensor, gscale: torch.Tensor,
+                           scale_mode: int = SCALE_REF240) -> torch.Tensor:
+    _need(codes, torch.uint8, "codes")
+    _need(scales, torch.uint8, "scales")
+    _need(gscale, torch.float32, "gscale")
+    n = codes.numel() * 2
+    nt = gscale.numel()
+    if n % nt:
+        raise ValueError("codes do not split into gscale.numel() tiles")
+    out = torch.empty(n, dtype=torch.float32, device=codes.device)
+    check("gdn_nvfp4_dequantize_tiles",
+          lib.gdn_nvfp4_dequantize_tiles(_ptr(codes), _ptr(scales), _ptr(gscale), nt, n // nt, _ptr(out),
+                                         scale_mode, _stream(codes)))
+    return out
+
+
+# ---- legacy op -------------------------------------------------------------------
+
+def legacy_state_update(S_data, S_scales, k, v, alpha: float, beta: float, d: int, out=None):
+    """launch_gdn_state_update through the C ABI (freshly allocated outputs, as
+    the reference op does, unless `out=(data, scales)` is given)."""
+    _need(S_data, torch.uint8, "S_data")
+    _need(S_scales, torch.uint8, "S_scales")
+    _need(k, torch.bfloat16, "k")
+    _need(v, torch.bfloat16, "v")
+    n = d * d
+    if S_data.numel() != n // 2 or S_scales.numel() != n // 16 or k.numel() != d or v.numel() != d:
+        raise ValueError("size mismatch")
+    if out is None:
+        out = (torch.empty(n // 2, dtype=torch.uint8, device=S_data.device),
+               torch.empty(n // 16, dtype=torch.uint8, device=S_data.device))
+    rc = lib.launch_gdn_state_update(_ptr(S_data), _ptr(S_scales), _ptr(k), _ptr(v), _ptr(out[0]), _ptr(out[1]),
+                                     float(alpha), float(beta), int(d), _stream(S_data))
+    check("launch_gdn_state_update", rc)
+    return out
+
+
+def legacy_ref_update(S_data, S_scales, k, v, alpha: float, beta: float, d: int) -> torch.Tensor:
+    """launch_gdn_ref: fp32 S' = alpha*S + beta*k v^T."""
+    out = torch.empty(d * d, dtype=torch.float32, device=S_data.device)
+    lib.launch_gdn_ref(_ptr(S_data), _ptr(S_scales), _ptr(k), _ptr(v), _ptr(out), float(alpha), float(beta),
+                       int(d), _stream(S_data))
+    return out
+
+
+def legacy_set_rounding(variant: int) -> int:
+    return lib.gdn_legacy_set_rounding(int(variant))
+
+
+# ---- decode ------------------------------------------------------------------------
+
+def decode(q, k, v, g, beta, slot_idx, pool, out=None, q_scale: float = 0.0, debug_y=None):
+    """One fused gated-delta-rule decode step over the NVFP4 pool `pool`
+    (gdn_b200.pool.NVFP4StatePool).  q, k: [B, HK, D] bf16; v: [B, HV, D] bf16;
+    g, beta: [B, HV] fp32; slot_idx: [B] int32.  Returns out [B, HV, D] bf16."""
+    B, HK, D = q.shape
+    HV = v.shape[1]
+    for t, name in ((q, "q"), (k, "k"), (v, "v")):
+        if t.dtype != torch.bfloat16 or not t.is_cuda or t.stride(-1) != 1 or t.stride(-2) != D:
+            raise ValueError(f"{name} must be CUDA bf16 with contiguous heads")
+    _need(g, torch.float32, "g")
+    _need(beta, torch.float32, "beta")
+    _need(slot_idx, torch.int32, "slot_idx")
+    if k.shape != (B, HK, D) or v.shape != (B, HV, D) or g.shape != (B, HV) or beta.shape != (B, HV):
+        raise ValueError("shape mismatch")
+    if pool.num_v_heads != HV or pool.head_dim != D:
+        raise ValueError("pool does not match the head layout")
+    if out is None:
+        out = torch.empty((B, HV, D), dtype=torch.bfloat16, device=q.device)
+    p = _capi.DecodeParams()
+    p.batch, p.num_k_heads, p.num_v_heads, p.head_dim = B, HK, HV, D
+    p.num_slots = pool.num_slots
+    p.q, p.k, p.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+    p.q_stride, p.k_stride, p.v_stride = q.stride(0), k.stride(0), v.stride(0)
+    p.g, p.beta, p.slot_idx = g.data_ptr(), beta.data_ptr(), slot_idx.data_ptr()
+    p.pool_codes, p.pool_scales, p.pool_gscale = pool.codes.data_ptr(), pool.scales.data_ptr(), pool.gscale.data_ptr()
+    p.out = out.data_ptr()
+    p.q_scale = q_scale
+    p.scale_mode = pool.scale_mode
+    p.gscale_den = pool.gscale_den
+    p.debug_y = _ptr(debug_y)
+    check("gdn_decode", lib.gdn_decode(ctypes.byref(p), _stream(q)))
+    return out
+
+
+# ---- pool ----------------------------------------------------------------------------
+
+def pool_gather(pool, slot_idx: torch.Tensor):
+    n = slot_idx.numel()
+    HV, D = pool.num_v_heads, pool.head_dim
+    codes = torch.empty((n, HV, D, D // 2), dtype=torch.uint8, device=pool.codes.device)
+    scales = torch.empty((n, HV, D, D // 16), dtype=torch.uint8, device=pool.codes.device)
+    gs = torch.empty((n, HV), dtype=torch.float32, device=pool.codes.device)
+    check("gdn_pool_gather",
+          lib.gdn_pool_gather(pool.codes.data_ptr(), pool.scales.data_ptr(), pool.gscale.data_ptr(), pool.num_slots,
+                              HV, D, slot_idx.data_ptr(), n, codes.data_ptr(), scales.data_ptr(), gs.data_ptr(),
+                              _stream(slot_idx)))
+    return codes, scales, gs
+
+
+def pool_scatter(pool, slot_idx: torch.Tensor, codes, scales, gs) -> None:
+    n = slot_idx.numel()
+    check("gdn_pool_scatter",
+          lib.gdn_pool_scatter(codes.data_ptr(), scales.data_ptr(), gs.data_ptr(), pool.num_slots, pool.num_v_heads,
+                               pool.head_dim, slot_idx.data_ptr(), n, pool.codes.data_ptr(),
+                               pool.scales.data_ptr(), pool.gscale.data_ptr(), _stream(slot_idx)))
+
+
+def device_status(clear: bool = True, device: torch.device | int | None = None) -> int:
+    """Reads (and clears) the library's device status word; synchronises."""
+    st = ctypes.c_uint32(0)
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        check("gdn_b200_device_status",
+              lib.gdn_b200_device_status(ctypes.byref(st), int(clear), torch.cuda.current_stream().cuda_stream))
+    return st.value
+
+
+def default_q_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)
+
+
+__all__ = [
+    "SCALE_REF240", "SCALE_FN448", "nvfp4_quantize", "nvfp4_dequantize", "nvfp4_quantize_tiles",
+    "nvfp4_dequantize_tiles", "legacy_state_update", "legacy_ref_update", "legacy_set_rounding", "decode",
+    "pool_gather", "pool_scatter", "device_status", "default_q_scale",
+]

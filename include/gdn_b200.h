@@ -1,0 +1,191 @@
+/*
+ * gdn_b200.h -- C ABI of libgdn_b200.so, the B200 (sm_100a) NVFP4 Gated
+ * DeltaNet state-update library.
+ *
+ * Conventions
+ *   - Plain C types only: device pointers, sizes, a cudaStream_t.  Every call
+ *     is stream-ordered and non-blocking: no allocation, no host
+ *     synchronisation, no host round trip (gdn_b200_device_status is the one
+ *     exception and says so).  The caller owns every buffer.
+ *   - Calls are stateless and safe from any host thread; ordering is per
+ *     stream.  Errors are integer status codes (GDN_OK == 0).
+ *   - bf16 arrays are IEEE bfloat16 (__nv_bfloat16 in C++, uint16_t bit
+ *     patterns in C).
+ *   - Device pointers handed to the bulk-copy (TMA) kernels must be 16-byte
+ *     aligned and rows of bf16 vectors must start on 16-byte boundaries
+ *     (strides that are multiples of 8 elements).
+ *
+ * NVFP4 state format (the reference's, src/kernel/gdn_state_update_ref.cu:16-18,
+ * plus a per-tile global scale): E2M1 codes two per byte, the even element in
+ * the low nibble; one E4M3-style scale byte per 16 contiguous elements; for the
+ * pooled GDN state one fp32 global scale per (slot, value head) tile.  A state
+ * tile is S[k][v] (d_k rows, d_v contiguous), so scale blocks run along d_v.
+ *
+ * Reference interfaces (paths in bojak83318/blackwell-kernel-sm_120):
+ *   launch_gdn_state_update   src/kernel/gdn_state_update_ref.cu:202-262,
+ *                             declared by src/ops/gdn_op.cu:32-40 and
+ *                             tests/test_gdn_correctness.cu:32-36
+ *   launch_gdn_ref            src/kernel/gdn_state_update_ref.cu:147-176
+ *   nvfp4 (de)quantise        src/kernel/gdn_state_update_ref.cu:75-141 (host)
+ *                             and :178-197 (device dequantise)
+ *   decode / prefill / pool   no counterpart in the reference (its only batched
+ *                             kernel, src/kernel/gdn_state_update.cu:112-182,
+ *                             is unreachable); the parameter blocks follow the
+ *                             batched layout of gdn_state_update.cu:65-75
+ */
+#ifndef GDN_B200_H_
+#define GDN_B200_H_
+
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+/* Symbols of this header are the library's only exports. */
+#if defined(__GNUC__)
+#define GDN_API __attribute__((visibility("default")))
+#else
+#define GDN_API
+#endif
+
+#ifdef __cplusplus
+#include <cuda_bf16.h>
+typedef __nv_bfloat16 gdn_bf16_t;
+extern "C" {
+#else
+typedef uint16_t gdn_bf16_t;
+#endif
+
+/* ---- status codes --------------------------------------------------------
+ * 0 and 1 keep the reference's meaning (gdn_state_update_ref.cu:214-217);
+ * 3 keeps "kernel launch failed" (:232-236).  The reference's 2/4/5/6
+ * (cudaMalloc, stream sync, D2H, H2D failures) cannot occur: nothing here
+ * allocates, synchronises or copies through the host. */
+#define GDN_OK 0
+#define GDN_ERR_ARGS 1        /* null pointer, non-positive or inconsistent size */
+#define GDN_ERR_LAUNCH 3      /* kernel launch failed (cudaGetLastError) */
+#define GDN_ERR_UNSUPPORTED 7 /* shape or mode outside what this build implements */
+#define GDN_ERR_ALIGN 8       /* pointer or stride not 16-byte aligned */
+#define GDN_ERR_CUDA 9        /* a CUDA runtime query failed */
+
+/* Device status bits, set by kernels and read by gdn_b200_device_status. */
+#define GDN_STATUS_WAIT_TIMEOUT 0x1u /* a bounded wait gave up; the kernel left early */
+#define GDN_STATUS_BAD_SLOT 0x2u     /* a slot index >= num_slots was skipped */
+
+/* Scale modes. */
+#define GDN_SCALE_REF240 0 /* the reference codec: scales saturate at 240 (0x77) */
+#define GDN_SCALE_FN448 1  /* reference rounding, E4M3FN range: saturate at 448 (0x7E) */
+
+/* ---- legacy op (kept byte-compatible) -------------------------------------- */
+
+/* One d x d state update S' = alpha*S + beta * k v^T, NVFP4 in and out, no
+ * global scale, reference quantiser (mode GDN_SCALE_REF240).  Same prototype
+ * and return codes as the reference (gdn_state_update_ref.cu:202-262); unlike
+ * it, this one runs entirely on the GPU, stream-ordered, with no cudaMalloc and
+ * no host synchronisation.  S_data [d*d/2], S_scales [d*d/16], k, v [d];
+ * requires d*d % 16 == 0.  In-place (out == in) is allowed. */
+GDN_API int launch_gdn_state_update(const uint8_t* S_data, const uint8_t* S_scales, const gdn_bf16_t* k,
+                            const gdn_bf16_t* v, uint8_t* S_out_data, uint8_t* S_out_scales,
+                            float alpha, float beta, int d, cudaStream_t stream);
+
+/* fp32 reference update (gdn_state_update_ref.cu:147-176): dequantise the
+ * NVFP4 state and write S_out = alpha*S + beta*k v^T in fp32 [d*d].  Same
+ * prototype (void); errors surface through cudaGetLastError as in the
+ * reference.  Fused into one kernel: no temporary buffer. */
+GDN_API void launch_gdn_ref(const uint8_t* S_data, const uint8_t* S_scales, const gdn_bf16_t* k,
+                    const gdn_bf16_t* v, float* S_out, float alpha, float beta, int d,
+                    cudaStream_t stream);
+
+/* Selects how the legacy update rounds alpha*s + (beta*k)*v:
+ * 0 = fmaf(alpha, s, (beta*k)*v), 1 = fmaf(beta*k, v, alpha*s), 2 = no FMA.
+ * Returns the previous setting.  The default matches the reference kernel as
+ * compiled for sm_100a. */
+GDN_API int gdn_legacy_set_rounding(int variant);
+
+/* ---- NVFP4 codec ----------------------------------------------------------- */
+
+/* Device twin of nvfp4_quantise_host (gdn_state_update_ref.cu:93-141): n % 16 == 0,
+ * codes [n/2], scales [n/16].  Bit-exact with the reference for every fp32
+ * input in mode GDN_SCALE_REF240. */
+GDN_API int gdn_nvfp4_quantize(const float* x, uint8_t* codes, uint8_t* scales, int64_t n,
+                       int32_t scale_mode, cudaStream_t stream);
+
+/* Device twin of nvfp4_dequantise_host (gdn_state_update_ref.cu:75-89; device
+ * form :178-197). */
+GDN_API int gdn_nvfp4_dequantize(const uint8_t* codes, const uint8_t* scales, float* out, int64_t n,
+                         int32_t scale_mode, cudaStream_t stream);
+
+/* Per-tile global scale (new): for each of num_tiles tiles of tile_elems
+ * (a multiple of 16) elements, gs = amax/gscale_den (1.0 for an all-zero tile),
+ * then the reference quantiser on y = x * (1/gs).  gscale_den <= 0 selects
+ * 6*240 (mode 0) or 6*448 (mode 1).  gscale [num_tiles]. */
+GDN_API int gdn_nvfp4_quantize_tiles(const float* x, int64_t num_tiles, int64_t tile_elems, uint8_t* codes,
+                             uint8_t* scales, float* gscale, int32_t scale_mode, float gscale_den,
+                             cudaStream_t stream);
+
+/* Inverse: out = (e2m1 * scale) * gs. */
+GDN_API int gdn_nvfp4_dequantize_tiles(const uint8_t* codes, const uint8_t* scales, const float* gscale,
+                               int64_t num_tiles, int64_t tile_elems, float* out,
+                               int32_t scale_mode, cudaStream_t stream);
+
+/* ---- fused recurrent decode (one token per sequence) ------------------------
+ * For each sequence b and value head h (key head h / (HV/HK)):
+ *   alpha = exp(g);  S_a = alpha*S;  u = S_a^T k;  w = beta*(v - u)
+ *   S' = S_a + k w^T;  out = q_scale * S'^T q
+ * S is the NVFP4 tile at pool slot slot_idx[b]; S' is written back in place
+ * with a fresh global scale.  A negative slot marks padding (out = 0, pool
+ * untouched); a slot >= num_slots is skipped the same way and flagged in the
+ * device status.  Non-negative slots must be distinct.  head_dim must be 128. */
+typedef struct gdn_decode_params {
+  int32_t batch;          /* B */
+  int32_t num_k_heads;    /* HK */
+  int32_t num_v_heads;    /* HV, a multiple of HK */
+  int32_t head_dim;       /* d_k = d_v */
+  int64_t num_slots;      /* pool slots */
+  const gdn_bf16_t* q;    /* [B, HK, D], sequence stride q_stride */
+  const gdn_bf16_t* k;    /* [B, HK, D], sequence stride k_stride */
+  const gdn_bf16_t* v;    /* [B, HV, D], sequence stride v_stride */
+  int64_t q_stride;       /* elements between sequences; 0 = HK*D */
+  int64_t k_stride;       /* 0 = HK*D */
+  int64_t v_stride;       /* 0 = HV*D */
+  const float* g;         /* [B, HV] log decay */
+  const float* beta;      /* [B, HV] */
+  const int32_t* slot_idx; /* [B] */
+  uint8_t* pool_codes;    /* [num_slots, HV, D, D/2] */
+  uint8_t* pool_scales;   /* [num_slots, HV, D, D/16] */
+  float* pool_gscale;     /* [num_slots, HV] */
+  gdn_bf16_t* out;        /* [B, HV, D] */
+  float q_scale;          /* <= 0 selects 1/sqrt(D) */
+  int32_t scale_mode;     /* GDN_SCALE_* */
+  float gscale_den;       /* <= 0 selects 6*saturation */
+  float* debug_y;         /* optional [B, HV, D, D]: the fp32 quantiser inputs */
+} gdn_decode_params;
+
+GDN_API int gdn_decode(const gdn_decode_params* params, cudaStream_t stream);
+
+/* ---- state pool ------------------------------------------------------------ */
+
+/* Copies tiles pool[slot_idx[i]] -> dense[i] for i < n (negative slot: the
+ * dense tile is zeroed).  Tile = HV heads of D x D states. */
+GDN_API int gdn_pool_gather(const uint8_t* pool_codes, const uint8_t* pool_scales, const float* pool_gscale,
+                    int64_t num_slots, int32_t num_v_heads, int32_t head_dim,
+                    const int32_t* slot_idx, int32_t n, uint8_t* dense_codes,
+                    uint8_t* dense_scales, float* dense_gscale, cudaStream_t stream);
+
+/* Copies dense[i] -> pool[slot_idx[i]] (negative slot: skipped). */
+GDN_API int gdn_pool_scatter(const uint8_t* dense_codes, const uint8_t* dense_scales,
+                     const float* dense_gscale, int64_t num_slots, int32_t num_v_heads,
+                     int32_t head_dim, const int32_t* slot_idx, int32_t n, uint8_t* pool_codes,
+                     uint8_t* pool_scales, float* pool_gscale, cudaStream_t stream);
+
+/* ---- library ----------------------------------------------------------------- */
+
+/* Reads (and with clear != 0 resets) the device status word of the current
+ * device after synchronising `stream`.  This call blocks the host. */
+GDN_API int gdn_b200_device_status(uint32_t* status_out, int clear, cudaStream_t stream);
+
+GDN_API const char* gdn_b200_error_string(int code);
+GDN_API const char* gdn_b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GDN_B200_H_ */

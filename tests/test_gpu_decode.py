@@ -1,0 +1,261 @@
+"""GPU parity of the fused NVFP4 gated-delta-rule decode (gdn_decode, through
+the C ABI) with the CPU oracle.
+
+* Exactness: the codes and scales the kernel writes are the reference
+  quantiser applied to the kernel's own fp32 quantiser inputs (debug_y),
+  bit for bit.
+* Per-step parity (teacher forced: both sides start each step from the same
+  pool): outputs and quantiser inputs agree to fp32 reduction-order error;
+  codes differ only where that error crosses a rounding boundary.
+* SQNR gate: over 64 free-running steps the GPU's outputs and final states,
+  against the unquantised f64 recurrence, are within 0.1 dB of (or better
+  than) the oracle's own quantised recurrence.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+HK, HV, D = 16, 32, 128
+QS = 1.0 / np.sqrt(D)
+
+
+def _pool(n_slots, mode, seed=1, std=0.02):
+    from gdn_b200 import NVFP4StatePool, workloads
+    states = workloads.initial_states(n_slots, HV, D, std=std, seed=seed)
+    pool = NVFP4StatePool.zeros(n_slots, HV, D, "cuda", scale_mode=mode)
+    pool.load_fp32(states.cuda())
+    return pool, states
+
+
+def _snap(pool):
+    return (pool.codes.cpu().numpy().copy(), pool.scales.cpu().numpy().copy(), pool.gscale.cpu().numpy().copy())
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def _inputs(B, steps, seed=0):
+    from gdn_b200 import workloads
+    return workloads.decode_steps(B, steps, HK, HV, D, seed=seed, device="cuda")
+
+
+def _gpu_step(pool, x, t, slot, debug=False):
+    from gdn_b200 import ops
+    y = torch.empty((slot.numel(), HV, D, D), dtype=torch.float32, device="cuda") if debug else None
+    o = ops.decode(x["q"][t], x["k"][t], x["v"][t], x["g"][t], x["beta"][t], slot, pool, debug_y=y)
+    torch.cuda.synchronize()
+    return o, y
+
+
+def _oracle_step(oracle_lib, snap, x, t, slot_np, mode):
+    codes, scales, gs = (a.copy() for a in snap)
+    o32, o16, y = oracle_lib.gdn_decode(_bits(x["q"][t]), _bits(x["k"][t]), _bits(x["v"][t]),
+                                        x["g"][t].cpu().numpy(), x["beta"][t].cpu().numpy(), slot_np,
+                                        codes, scales, gs, QS, mode, want_y=True)
+    return o32, y, (codes, scales, gs)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_pool_initialisation_bit_exact(cuda, oracle_lib, mode):
+    pool, states = _pool(4, mode)
+    c0, s0, g0, _ = oracle_lib.quantise_tiles(states.numpy().reshape(-1), D * D, mode)
+    codes, scales, gs = _snap(pool)
+    np.testing.assert_array_equal(gs.reshape(-1).view(np.uint32), g0.view(np.uint32))
+    np.testing.assert_array_equal(scales.reshape(-1), s0)
+    np.testing.assert_array_equal(codes.reshape(-1), c0)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_decode_teacher_forced(cuda, oracle_lib, mode):
+    B, steps = 4, 6
+    pool, _ = _pool(8, mode)
+    slot = torch.tensor([5, 2, 7, 0], dtype=torch.int32, device="cuda")
+    slot_np = slot.cpu().numpy()
+    x = _inputs(B, steps)
+    for t in range(steps):
+        snap = _snap(pool)
+        o, y = _gpu_step(pool, x, t, slot, debug=True)
+        o_ref, y_ref, (c_ref, s_ref, g_ref) = _oracle_step(oracle_lib, snap, x, t, slot_np, mode)
+        codes, scales, gs = _snap(pool)
+        y_np = y.cpu().numpy()
+        for b in range(B):
+            s = int(slot_np[b])
+            # exactness: codes/scales == reference quantiser(kernel's own y)
+            c2, s2 = oracle_lib.quantise(y_np[b].reshape(-1), mode)
+            np.testing.assert_array_equal(codes[s].reshape(-1), c2)
+            np.testing.assert_array_equal(scales[s].reshape(-1), s2)
+            # global scale: amax(S') / gden, within fp32 reduction error
+            np.testing.assert_allclose(gs[s], g_ref[s], rtol=2e-6)
+        # y: the same fp32 state up to reduction order
+        gden = 6.0 * (448.0 if mode else 240.0)
+        assert np.abs(y_np - y_ref).max() <= 2e-4 * gden
+        frac = float((codes != c_ref).mean())
+        assert frac < 2e-3, frac
+        # outputs: bf16 rounding of the same fp32 value
+        o_np = o.float().cpu().numpy()
+        err = np.abs(o_np - o_ref)
+        assert (err <= 6e-3 * np.abs(o_ref) + 2e-4 * np.abs(o_ref).max()).all(), err.max()
+        # unused slots untouched
+        for s in (1, 3, 4, 6):
+            np.testing.assert_array_equal(codes[s], snap[0][s])
+
+
+def _f64_reference(states0, x, slot_np, steps):
+    """Unquantised f64 recurrence per (sequence, head) from the fp32 initial states."""
+    from oracle import bindings as ob
+    B = slot_np.size
+    o = np.zeros((steps, B, HV, D))
+    S_end = np.zeros((B, HV, D, D))
+    q = x["q"][:steps].float().cpu().numpy()
+    k = x["k"][:steps].float().cpu().numpy()
+    v = x["v"][:steps].float().cpu().numpy()
+    g = x["g"][:steps].cpu().numpy()
+    be = x["beta"][:steps].cpu().numpy()
+    for b in range(B):
+        for h in range(HV):
+            hk = h // (HV // HK)
+            ob_, S = ob.recurrent_f64(states0[slot_np[b], h].astype(np.float64), q[:, b, hk], k[:, b, hk], v[:, b, h],
+                                      g[:, b, h], be[:, b, h], QS)
+            o[:, b, h] = ob_
+            S_end[b, h] = S
+    return o, S_end
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_sqnr_gate_64_steps(cuda, oracle_lib, mode):
+    B, steps = 4, 64
+    pool, states = _pool(4, mode)
+    slot = torch.tensor([2, 0, 3, 1], dtype=torch.int32, device="cuda")
+    slot_np = slot.cpu().numpy()
+    x = _inputs(B, steps, seed=10)
+    o_ref, S_ref = _f64_reference(states.numpy(), x, slot_np, steps)
+    # oracle quantised trajectory
+    codes, scales, gs = _snap(pool)
+    o_orc = np.zeros_like(o_ref)
+    for t in range(steps):
+        o32, _, _ = oracle_lib.gdn_decode(_bits(x["q"][t]), _bits(x["k"][t]), _bits(x["v"][t]),
+                                          x["g"][t].cpu().numpy(), x["beta"][t].cpu().numpy(), slot_np,
+                                          codes, scales, gs, QS, mode)
+        o_orc[t] = o32
+    S_orc = oracle_lib.dequantise_tiles(codes.reshape(-1), scales.reshape(-1), gs.reshape(-1), mode).reshape(4, HV, D, D)
+    # GPU quantised trajectory
+    o_gpu = np.zeros_like(o_ref)
+    for t in range(steps):
+        o, _ = _gpu_step(pool, x, t, slot)
+        o_gpu[t] = o.float().cpu().numpy()
+    S_gpu = pool.dequantize().cpu().numpy()
+    sq = {
+        "o_oracle": oracle_lib.sqnr_db(o_ref, o_orc), "o_gpu": oracle_lib.sqnr_db(o_ref, o_gpu),
+        "S_oracle": oracle_lib.sqnr_db(S_ref, S_orc[slot_np]), "S_gpu": oracle_lib.sqnr_db(S_ref, S_gpu[slot_np]),
+    }
+    print(f"SQNR mode {mode}: {sq}")
+    assert sq["o_gpu"] >= sq["o_oracle"] - 0.1, sq
+    assert sq["S_gpu"] >= sq["S_oracle"] - 0.1, sq
+
+
+def test_padding_and_out_of_range_slots(cuda, oracle_lib):
+    from gdn_b200 import ops
+    pool, _ = _pool(4, 0)
+    ops.device_status(clear=True)
+    before = _snap(pool)
+    slot = torch.tensor([-1, 1, 9, 3], dtype=torch.int32, device="cuda")
+    x = _inputs(4, 1)
+    o, _ = _gpu_step(pool, x, 0, slot)
+    o_np = o.float().cpu().numpy()
+    assert (o_np[0] == 0).all() and (o_np[2] == 0).all()
+    assert np.abs(o_np[1]).max() > 0
+    after = _snap(pool)
+    for s in (0, 2):
+        np.testing.assert_array_equal(after[0][s], before[0][s])
+        np.testing.assert_array_equal(after[1][s], before[1][s])
+    assert (after[0][1] != before[0][1]).any()
+    st = ops.device_status(clear=True)
+    assert st & 0x2  # GDN_STATUS_BAD_SLOT
+    assert ops.device_status(clear=True) == 0
+
+
+def test_strided_qkv_views(cuda):
+    """q, k, v as views of one fused projection row [B, (2HK + HV) * D]."""
+    from gdn_b200 import ops
+    B = 8
+    x = _inputs(B, 1, seed=4)
+    fused = torch.cat([x["q"][0].reshape(B, -1), x["k"][0].reshape(B, -1), x["v"][0].reshape(B, -1)], dim=1)
+    qv = fused[:, :HK * D].view(B, HK, D)
+    kv = fused[:, HK * D:2 * HK * D].view(B, HK, D)
+    vv = fused[:, 2 * HK * D:].view(B, HV, D)
+    slot = torch.arange(B, dtype=torch.int32, device="cuda")
+    p1, _ = _pool(B, 0)
+    p2, _ = _pool(B, 0)
+    o1 = ops.decode(x["q"][0], x["k"][0], x["v"][0], x["g"][0], x["beta"][0], slot, p1)
+    o2 = ops.decode(qv, kv, vv, x["g"][0], x["beta"][0], slot, p2)
+    assert torch.equal(o1, o2)
+    assert torch.equal(p1.codes, p2.codes) and torch.equal(p1.scales, p2.scales)
+    assert torch.equal(p1.gscale, p2.gscale)
+
+
+def test_deterministic_bytes(cuda):
+    from gdn_b200 import ops
+    B = 64
+    x = _inputs(B, 1, seed=5)
+    slot = torch.arange(B, dtype=torch.int32, device="cuda")
+    outs = []
+    for _ in range(2):
+        p, _ = _pool(B, 0)
+        o = ops.decode(x["q"][0], x["k"][0], x["v"][0], x["g"][0], x["beta"][0], slot, p)
+        outs.append((o.clone(), p.codes.clone(), p.scales.clone(), p.gscale.clone()))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+
+
+def test_full_size_batch256_with_random_slots(cuda, oracle_lib):
+    """Batch-256 decode step over a 2048-slot pool addressed through a seeded
+    random permutation: bit-exact codes against the reference quantiser on
+    every tile, and teacher-forced parity on 48 sampled tiles."""
+    from gdn_b200 import NVFP4StatePool, ops, workloads
+    B, n_slots = 256, 2048
+    pool = NVFP4StatePool.zeros(n_slots, HV, D, "cuda")
+    slot = workloads.slot_permutation(B, n_slots, seed=3).cuda()
+    slot_np = slot.cpu().numpy()
+    states = workloads.initial_states(B, HV, D, seed=7).cuda()
+    pool.load_fp32(states, slot)
+    x = _inputs(B, 1, seed=6)
+    snap_c = pool.codes[slot.long()].cpu().numpy()
+    snap_s = pool.scales[slot.long()].cpu().numpy()
+    snap_g = pool.gscale[slot.long()].cpu().numpy()
+    o, y = _gpu_step(pool, x, 0, slot, debug=True)
+    codes = pool.codes[slot.long()].cpu().numpy()
+    scales = pool.scales[slot.long()].cpu().numpy()
+    y_np = y.cpu().numpy()
+    c2, s2 = oracle_lib.quantise(y_np.reshape(-1), 0)
+    np.testing.assert_array_equal(scales.reshape(-1), s2)
+    np.testing.assert_array_equal(codes.reshape(-1), c2)
+    # sampled teacher-forced parity: oracle on a compact pool of the sampled sequences
+    pick = np.random.default_rng(0).choice(B, 48, replace=False)
+    sub_slot = np.arange(48, dtype=np.int32)
+    cc, ss, gg = snap_c[pick].copy(), snap_s[pick].copy(), snap_g[pick].copy()
+    sel = torch.from_numpy(pick).cuda().long()
+    o32, _, y_ref = oracle_lib.gdn_decode(_bits(x["q"][0][sel]), _bits(x["k"][0][sel]), _bits(x["v"][0][sel]),
+                                          x["g"][0][sel].cpu().numpy(), x["beta"][0][sel].cpu().numpy(), sub_slot,
+                                          cc, ss, gg, QS, 0, want_y=True)
+    o_np = o.float().cpu().numpy()[pick]
+    assert np.abs(o_np - o32).max() <= 6e-3 * np.abs(o32).max()
+    assert np.abs(y_np[pick] - y_ref).max() <= 2e-4 * 1440.0
+    assert float((codes[pick] != cc).mean()) < 2e-3
+
+
+def test_torch_op_decode_matches_c_abi(cuda):
+    from gdn_b200 import gdn_op, ops
+    B = 16
+    x = _inputs(B, 1, seed=8)
+    slot = torch.arange(B, dtype=torch.int32, device="cuda")
+    p1, _ = _pool(B, 0)
+    p2, _ = _pool(B, 0)
+    o1 = ops.decode(x["q"][0], x["k"][0], x["v"][0], x["g"][0], x["beta"][0], slot, p1)
+    o2 = gdn_op.decode(x["q"][0], x["k"][0], x["v"][0], x["g"][0], x["beta"][0], slot, p2)
+    assert torch.equal(o1, o2)
+    assert torch.equal(p1.codes, p2.codes)
