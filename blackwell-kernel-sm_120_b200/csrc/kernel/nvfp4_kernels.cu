@@ -211,7 +211,10 @@ __global__ void __launch_bounds__(kThreads) legacy_update_kernel(const uint8_t* 
   }
 }
 
-int g_legacy_variant = 0;
+// fmaf(beta*k, v, alpha*s): the rounding of the reference's compiled update
+// line, found by comparing every variant bit for bit with the reference's
+// launch_gdn_ref on a B200 (tests/test_gpu_legacy.py).
+int g_legacy_variant = 1;
 
 template <bool kOutF32>
 int launch_legacy(const uint8_t* S_data, const uint8_t* S_scales, const __nv_bfloat16* k,
