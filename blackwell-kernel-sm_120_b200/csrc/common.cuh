@@ -61,6 +61,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As mbar_try_wait, but the hardware may suspend the thread for up to
+// `suspend_ns` while the phase is incomplete (it resumes when the phase
+// completes), so a waiting thread issues few instructions.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t suspend_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete; false after
 // `timeout_ns` without completion (the caller reports and leaves).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
@@ -68,9 +81,18 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_suspend(bar, parity, 100000u)) return true;
     if (globaltimer_ns() - t0 > timeout_ns) return false;
   }
+}
+
+// CTA-wide bounded wait: thread 0 waits, the others are parked at the
+// barrier (no instruction issue).  Uniform result; must be reached by every
+// thread of the CTA.
+__device__ __forceinline__ bool mbar_wait_cta(uint64_t* bar, uint32_t parity, uint64_t timeout_ns = kWaitTimeoutNs) {
+  bool ok = true;
+  if (threadIdx.x == 0) ok = mbar_wait_bounded(bar, parity, timeout_ns);
+  return !__syncthreads_or(!ok);
 }
 
 // 1-D bulk copy global -> shared, completing `bytes` on the mbarrier.

@@ -112,7 +112,7 @@ __host__ __device__ inline uint32_t scale_encode(float x, int mode) {
 }
 
 // Local block scale input: amax/6, or 1.0 for an all-zero block
-// (gdn_state_update_ref.cu:106-107).
+// (gdn_state_update_ref.cu:106-107).  The division is IEEE round-to-nearest.
 __host__ __device__ inline float local_scale(float amax) {
 #ifdef __CUDA_ARCH__
   return (amax > 0.0f) ? __fdiv_rn(amax, 6.0f) : 1.0f;
@@ -159,6 +159,27 @@ constexpr float kE2M1TieEps = 4.335e-8f;
 
 #ifdef __CUDACC__
 __device__ __forceinline__ float e2m1_nudge(float v) { return __fmaf_rn(v, -kE2M1TieEps, v); }
+
+// amax/6 in three operations (Markstein's FMA correction of a quotient: q0 =
+// a*RN(1/6), r = a - 6*q0 exactly, q = q0 + r*RN(1/6)).  Checked against IEEE
+// division for every positive finite float: identical for a >= 2^-125; below
+// that the quotient is subnormal and may differ in its last bits, but every
+// such quotient (< 2^-127) encodes to scale code 0 either way, so the scale
+// byte -- the only consumer -- is identical for all inputs.
+__device__ __forceinline__ float div6_for_scale(float a) {
+  const float y = 0.16666667163372039795f;  // RN(1/6)
+  const float q0 = __fmul_rn(a, y);
+  const float r = __fmaf_rn(-q0, 6.0f, a);
+  return __fmaf_rn(r, y, q0);
+}
+
+__device__ __forceinline__ float local_scale_fast(float amax) {
+  return (amax > 0.0f) ? div6_for_scale(amax) : 1.0f;
+}
+
+__device__ __forceinline__ float2 e2m1_nudge2(float2 v) {
+  return __ffma2_rn(v, make_float2(-kE2M1TieEps, -kE2M1TieEps), v);
+}
 
 // Two fp32 -> one byte: low nibble from `lo`, high nibble from `hi`.
 __device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
@@ -210,6 +231,42 @@ __device__ __forceinline__ float absmax_nan(float a, float b) {
   return r;
 }
 
+// Exact path: reference semantics (NaN-ignoring amax, literal encoder).  Kept
+// out of line: only blocks holding NaN/inf or huge ratios reach it.
+static __device__ __noinline__ uint32_t quantize16_exact(const float* y, int mode, uint32_t& w0, uint32_t& w1) {
+  float amax = 0.0f;
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(y[i]));
+  const uint32_t sc = scale_encode(local_scale(amax), mode);
+  const float inv = scale_inverse(scale_decode(sc, mode));
+  uint32_t c[2] = {0u, 0u};
+  for (int i = 0; i < 16; ++i) c[i >> 3] |= e2m1_encode_exact(__fmul_rn(y[i], inv)) << (4 * (i & 7));
+  w0 = c[0];
+  w1 = c[1];
+  return sc;
+}
+
+// The same exact path on register pairs (y[p] = elements 2p, 2p+1), inline so
+// that a kernel keeping its state in registers needs no call (and no spills)
+// for the rare non-finite block.
+__device__ __forceinline__ uint32_t quantize16_exact_pairs(const float2 (&y)[8], int mode, uint32_t& w0,
+                                                           uint32_t& w1) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int p = 0; p < 8; ++p) amax = fmaxf(amax, fmaxf(fabsf(y[p].x), fabsf(y[p].y)));
+  const uint32_t sc = scale_encode(local_scale(amax), mode);
+  const float inv = scale_inverse(scale_decode(sc, mode));
+  uint32_t c0 = 0u, c1 = 0u;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    c0 |= (e2m1_encode_exact(__fmul_rn(y[p].x, inv)) | (e2m1_encode_exact(__fmul_rn(y[p].y, inv)) << 4)) << (8 * p);
+    c1 |= (e2m1_encode_exact(__fmul_rn(y[p + 4].x, inv)) | (e2m1_encode_exact(__fmul_rn(y[p + 4].y, inv)) << 4))
+          << (8 * p);
+  }
+  w0 = c0;
+  w1 = c1;
+  return sc;
+}
+
 // Quantise 16 fp32 inputs (the reference quantiser's block) to 8 code bytes and
 // one scale byte.  `amax_nan` is the NaN-propagating |max| of the block.  The
 // fast path (hardware converter + tie nudge) is exact while the block is finite
@@ -235,18 +292,7 @@ __device__ __forceinline__ uint32_t quantize16(const float* y, float amax_nan, i
     w1 = cvt_e2m1x8(n + 8);
     return sc;
   }
-  // Exact path: reference semantics (NaN-ignoring amax, literal encoder).
-  float amax = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(y[i]));
-  sc = scale_encode(local_scale(amax), mode);
-  inv = scale_inverse(scale_decode(sc, mode));
-  uint32_t c[2] = {0u, 0u};
-#pragma unroll
-  for (int i = 0; i < 16; ++i) c[i >> 3] |= e2m1_encode_exact(y[i] * inv) << (4 * (i & 7));
-  w0 = c[0];
-  w1 = c[1];
-  return sc;
+  return quantize16_exact(y, mode, w0, w1);
 }
 #endif  // __CUDACC__
 

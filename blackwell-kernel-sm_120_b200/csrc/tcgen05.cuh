@@ -1,0 +1,184 @@
+// tcgen05.cuh -- thin wrappers over the sm_100a tensor-core (tcgen05) and
+// tensor-memory (TMEM) instructions used by the GDN kernels.
+//
+// Conventions (PTX ISA 8.7/8.8, CUDA 12.9):
+//   * TMEM address = (lane << 16) | column; a CTA allocates a power-of-two
+//     number of 32-bit columns (>= 32) across all 128 lanes.
+//   * Shared-memory matrix descriptor (64 bit): start address >> 4 in bits
+//     0-13, leading-dimension byte offset >> 4 in 16-29, stride-dimension byte
+//     offset >> 4 in 32-45, version 1 in bit 46, layout (swizzle) in 61-63.
+//     Only the no-swizzle "interleaved" K-major layout is used here: 8-row x
+//     16-byte core matrices, rows 16 B apart, SBO = byte distance between
+//     consecutive 8-row groups, LBO = byte distance between the two 16-byte
+//     K chunks one MMA consumes.
+//   * All MMAs are issued by one thread; completion is signalled through
+//     tcgen05.commit on an mbarrier.
+#pragma once
+
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace gdn {
+namespace tc {
+
+#ifdef __CUDACC__
+
+__device__ __forceinline__ uint64_t smem_desc(const void* base, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  const uint64_t addr = smem_u32(base);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;  // descriptor version for sm_100
+  // base offset 0, legacy LBO mode, layout type 0 (no swizzle)
+  return d;
+}
+
+// Instruction descriptor, block-scaled E2M1 x E2M1 (kind::mxf4nvf4), UE4M3
+// scale factors, fp32 accumulate, K-major A and B, K = 64 per instruction.
+__host__ __device__ constexpr uint32_t idesc_mxf4nvf4(int M, int N) {
+  return (1u << 7)                         // A format: E2M1
+         | (1u << 10)                      // B format: E2M1
+         | ((uint32_t)(N >> 3) << 17)      // N
+         | (0u << 23)                      // scale format UE4M3
+         | ((uint32_t)(M >> 4) << 24);     // M
+}
+
+// Instruction descriptor, kind::tf32 (fp32 operands read as tf32), fp32
+// accumulate, K-major A and B, K = 8 per instruction.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+  return (1u << 4)                         // D format: F32
+         | (2u << 7)                       // A format: TF32
+         | (2u << 10)                      // B format: TF32
+         | ((uint32_t)(N >> 3) << 17)
+         | ((uint32_t)(M >> 4) << 24);
+}
+
+// Instruction descriptor, kind::f16 with bf16 operands, fp32 accumulate,
+// K-major A and B, K = 16 per instruction.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ---- TMEM allocation (one warp) ----------------------------------------------------
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// ---- ordering ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Generic-proxy shared-memory writes -> visible to the async proxy (MMA, cp).
+__device__ __forceinline__ void fence_smem_to_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Arrives once on `bar` when every tcgen05 operation this thread issued so far
+// has completed.
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// ---- MMAs (single thread) ----------------------------------------------------------------
+
+__device__ __forceinline__ void mma_mxf4nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
+      "  tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p; }" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// A from TMEM (fp32 bits read as tf32), B from shared memory.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
+      "  tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p; }" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// A and B from shared memory.
+__device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
+      "  tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
+      "  tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Copies a 32-row x 128-bit matrix from shared memory to TMEM, replicated into
+// all four 32-lane subpartitions (the scale-factor layout of block-scaled MMAs).
+__device__ __forceinline__ void cp_32x128b_warpx4(uint32_t taddr, uint64_t src_desc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src_desc) : "memory");
+}
+
+// ---- TMEM -> registers (whole warp; lanes = the warp's 32-lane subpartition) -------
+
+__device__ __forceinline__ void ld_32x32b_x2(uint32_t taddr, float& a, float& b) {
+  uint32_t r0, r1;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(taddr));
+  a = __uint_as_float(r0);
+  b = __uint_as_float(r1);
+}
+
+// 32 consecutive columns of this thread's lane.
+__device__ __forceinline__ void ld_32x32b_x32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---- TMA tensor load (no multicast) -----------------------------------------------------------
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+#endif  // __CUDACC__
+
+}  // namespace tc
+}  // namespace gdn
