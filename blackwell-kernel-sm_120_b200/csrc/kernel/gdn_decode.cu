@@ -42,6 +42,7 @@
 #include "../common.cuh"
 #include "../intrinsics/nvfp4_codec.cuh"
 #include "../tcgen05.cuh"
+#include "tile_requant.cuh"
 
 namespace gdn {
 namespace {
@@ -406,41 +407,12 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const DecodeArg
     for (int w = 1; w < kWarps; ++w) amax = fmaxf(amax, sm.amax[w]);
     const float gs_new = (amax > 0.0f) ? __fdiv_rn(amax, a.gden) : 1.0f;
     const float inv_gs = __frcp_rn(gs_new);
-    const float2 r2 = make_float2(inv_gs, inv_gs);
 
     // ---- 5: requantise this thread's four blocks, store ----
     uint32_t words[8];
-    uint32_t scw = 0;
-#pragma unroll
-    for (int blk = 0; blk < 4; ++blk) {
-      float2 y[8];
-#pragma unroll
-      for (int p = 0; p < 8; ++p) y[p] = __fmul2_rn(x[8 * blk + p], r2);
-      // max |y| of the block = RN(max |S'| * inv_gs): rounding is monotone.
-      const float am_y = __fmul_rn(am[blk], inv_gs);
-      uint32_t w0, w1, sc;
-      if (am_y <= 3.0e38f) {
-        sc = scale_encode(local_scale_fast(am_y), kMode);
-        const float inv = sm.inv_tab[sc];
-        const float2 inv2 = make_float2(inv, inv), zero2 = make_float2(0.0f, 0.0f);
-        float2 nn[8];
-#pragma unroll
-        for (int p = 0; p < 8; ++p) nn[p] = e2m1_nudge2(__ffma2_rn(y[p], inv2, zero2));
-        w0 = cvt_e2m1x8(reinterpret_cast<const float*>(nn));
-        w1 = cvt_e2m1x8(reinterpret_cast<const float*>(nn + 4));
-      } else {  // NaN or inf in the block: exact scalar path
-        sc = quantize16_exact_pairs(y, kMode, w0, w1);
-      }
-      words[2 * blk] = w0;
-      words[2 * blk + 1] = w1;
-      scw |= sc << (8 * blk);
-      if (a.debug_y) {
-        float4* dy = reinterpret_cast<float4*>(a.debug_y + (((int64_t)b * a.HV + h) * kD + row) * kD + 64 * half +
-                                               16 * blk);
-#pragma unroll
-        for (int p = 0; p < 4; ++p) dy[p] = make_float4(y[2 * p].x, y[2 * p].y, y[2 * p + 1].x, y[2 * p + 1].y);
-      }
-    }
+    uint32_t scw;
+    requant_half_row<kMode>(x, am, inv_gs, sm.inv_tab, words, scw,
+                            a.debug_y ? a.debug_y + (((int64_t)b * a.HV + h) * kD + row) * kD + 64 * half : nullptr);
     uint4* dst = reinterpret_cast<uint4*>(a.pool_codes + cur.pt * kCodeBytes + row * 64 + 32 * half);
     dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
     dst[1] = make_uint4(words[4], words[5], words[6], words[7]);

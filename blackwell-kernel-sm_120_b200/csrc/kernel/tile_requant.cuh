@@ -1,0 +1,83 @@
+// tile_requant.cuh -- requantisation of one 64-element half row of a 128 x 128
+// NVFP4 state tile, shared by the decode and prefill kernels.
+//
+// A CTA of 256 threads holds the tile as 128 rows x 2 halves; each thread owns
+// x[0..31] = 64 consecutive fp32 elements (pairs) of one row, i.e. four whole
+// 16-element scale blocks.  The tile's global scale is gs = amax / gden
+// (1.0 for an all-zero tile) and every block goes through the reference block
+// quantiser (src/kernel/gdn_state_update_ref.cu:93-141) applied to
+// y = x * RN(1/gs): local scale amax_blk / 6, scale byte by the reference
+// encoder, E2M1 nearest with ties to the smaller magnitude.
+#pragma once
+
+#include <cstdint>
+
+#include "../intrinsics/nvfp4_codec.cuh"
+
+namespace gdn {
+
+// Per-block max |x| of the four blocks (NaN ignored, as the reference's fmaxf
+// scan does) and their maximum.  am[blk] may be NaN-free only; the return
+// value feeds the tile amax.
+__device__ __forceinline__ float block_amax4(const float2 (&x)[32], float (&am)[4]) {
+  float tmax = 0.0f;
+#pragma unroll
+  for (int blk = 0; blk < 4; ++blk) {
+    float mx = absmax_nan(x[8 * blk].x, x[8 * blk].y);
+#pragma unroll
+    for (int p = 1; p < 8; ++p) mx = absmax_nan(absmax_nan(mx, x[8 * blk + p].x), x[8 * blk + p].y);
+    am[blk] = fabsf(mx);
+    float ok_max = am[blk];
+    if (isnan(ok_max)) {
+      ok_max = 0.0f;
+#pragma unroll
+      for (int p = 0; p < 8; ++p) ok_max = fmaxf(ok_max, fmaxf(fabsf(x[8 * blk + p].x), fabsf(x[8 * blk + p].y)));
+    }
+    tmax = fmaxf(tmax, ok_max);
+  }
+  return tmax;
+}
+
+// Quantises the four blocks of x with the tile's inverse global scale.
+// am[blk] = max |x| of block blk as from block_amax4 (NaN when the block
+// holds one).  inv_tab[s] = 1 / decode(s) for every scale byte s.  Writes the
+// 32 code bytes (8 words, element order) and the four scale bytes (one word,
+// block order); debug_row, when set, receives the 64 fp32 quantiser inputs.
+template <int kMode>
+__device__ __forceinline__ void requant_half_row(const float2 (&x)[32], const float (&am)[4], float inv_gs,
+                                                 const float* inv_tab, uint32_t (&words)[8], uint32_t& scw,
+                                                 float* debug_row) {
+  const float2 r2 = make_float2(inv_gs, inv_gs);
+  scw = 0;
+#pragma unroll
+  for (int blk = 0; blk < 4; ++blk) {
+    float2 y[8];
+#pragma unroll
+    for (int p = 0; p < 8; ++p) y[p] = __fmul2_rn(x[8 * blk + p], r2);
+    // max |y| of the block = RN(max |x| * inv_gs): rounding is monotone.
+    const float am_y = __fmul_rn(am[blk], inv_gs);
+    uint32_t w0, w1, sc;
+    if (am_y <= 3.0e38f) {
+      sc = scale_encode(local_scale_fast(am_y), kMode);
+      const float inv = inv_tab[sc];
+      const float2 inv2 = make_float2(inv, inv), zero2 = make_float2(0.0f, 0.0f);
+      float2 nn[8];
+#pragma unroll
+      for (int p = 0; p < 8; ++p) nn[p] = e2m1_nudge2(__ffma2_rn(y[p], inv2, zero2));
+      w0 = cvt_e2m1x8(reinterpret_cast<const float*>(nn));
+      w1 = cvt_e2m1x8(reinterpret_cast<const float*>(nn + 4));
+    } else {  // NaN or inf in the block: exact scalar path
+      sc = quantize16_exact_pairs(y, kMode, w0, w1);
+    }
+    words[2 * blk] = w0;
+    words[2 * blk + 1] = w1;
+    scw |= sc << (8 * blk);
+    if (debug_row) {
+      float4* dy = reinterpret_cast<float4*>(debug_row + 16 * blk);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) dy[p] = make_float4(y[2 * p].x, y[2 * p].y, y[2 * p + 1].x, y[2 * p + 1].y);
+    }
+  }
+}
+
+}  // namespace gdn

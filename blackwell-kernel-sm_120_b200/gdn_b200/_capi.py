@@ -77,7 +77,7 @@ class PrefillParams(ctypes.Structure):
         ("pool_codes", _p), ("pool_scales", _p), ("pool_gscale", _p),
         ("out", _p),
         ("q_scale", _f32), ("scale_mode", _i32), ("gscale_den", _f32),
-        ("workspace", _p), ("workspace_bytes", _i64),
+        ("debug_y", _p),
     ]
 
 

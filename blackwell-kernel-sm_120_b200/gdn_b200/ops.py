@@ -159,6 +159,61 @@ def decode(q, k, v, g, beta, slot_idx, pool, out=None, q_scale: float = 0.0, deb
     return out
 
 
+def prefill(q, k, v, g, beta, cu_seqlens, pool=None, slot_idx=None, has_initial_state=None, out=None,
+            q_scale: float = 0.0, debug_y=None):
+    """Chunked gated-delta-rule prefill of packed variable-length sequences.
+    q, k: [T, HK, D] bf16; v: [T, HV, D] bf16; g, beta: [T, HV] fp32;
+    cu_seqlens: [N + 1] int32 (CUDA).  With `pool` and `slot_idx` ([N] int32),
+    sequence n starts from the pool state at slot_idx[n] when
+    has_initial_state[n] (bool [N]) is set, from zero otherwise, and its final
+    state is written back to that slot.  Returns out [T, HV, D] bf16."""
+    T, HK, D = q.shape
+    HV = v.shape[1]
+    for t, name in ((q, "q"), (k, "k"), (v, "v")):
+        if t.dtype != torch.bfloat16 or not t.is_cuda or t.stride(-1) != 1 or t.stride(-2) != D:
+            raise ValueError(f"{name} must be CUDA bf16 with contiguous heads")
+    _need(g, torch.float32, "g")
+    _need(beta, torch.float32, "beta")
+    _need(cu_seqlens, torch.int32, "cu_seqlens")
+    if k.shape != (T, HK, D) or v.shape != (T, HV, D) or g.shape != (T, HV) or beta.shape != (T, HV):
+        raise ValueError("shape mismatch")
+    N = cu_seqlens.numel() - 1
+    if N < 0:
+        raise ValueError("cu_seqlens needs N + 1 entries")
+    if slot_idx is not None:
+        if pool is None:
+            raise ValueError("slot_idx needs a pool")
+        _need(slot_idx, torch.int32, "slot_idx")
+        if slot_idx.numel() != N:
+            raise ValueError("slot_idx must have one entry per sequence")
+        if pool.num_v_heads != HV or pool.head_dim != D:
+            raise ValueError("pool does not match the head layout")
+    if has_initial_state is not None:
+        _need(has_initial_state, torch.bool, "has_initial_state")
+        if has_initial_state.numel() != N:
+            raise ValueError("has_initial_state must have one entry per sequence")
+    if out is None:
+        out = torch.empty((T, HV, D), dtype=torch.bfloat16, device=q.device)
+    p = _capi.PrefillParams()
+    p.num_seqs, p.num_k_heads, p.num_v_heads, p.head_dim = N, HK, HV, D
+    p.total_tokens = T
+    p.q, p.k, p.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+    p.q_stride, p.k_stride, p.v_stride = q.stride(0), k.stride(0), v.stride(0)
+    p.g, p.beta, p.cu_seqlens = g.data_ptr(), beta.data_ptr(), cu_seqlens.data_ptr()
+    p.has_initial_state = _ptr(has_initial_state)
+    if slot_idx is not None:
+        p.num_slots = pool.num_slots
+        p.slot_idx = slot_idx.data_ptr()
+        p.pool_codes, p.pool_scales = pool.codes.data_ptr(), pool.scales.data_ptr()
+        p.pool_gscale = pool.gscale.data_ptr()
+        p.scale_mode, p.gscale_den = pool.scale_mode, pool.gscale_den
+    p.out = out.data_ptr()
+    p.q_scale = q_scale
+    p.debug_y = _ptr(debug_y)
+    check("gdn_prefill", lib.gdn_prefill(ctypes.byref(p), _stream(q)))
+    return out
+
+
 # ---- pool ----------------------------------------------------------------------------
 
 def pool_gather(pool, slot_idx: torch.Tensor):

@@ -69,6 +69,7 @@ typedef uint16_t gdn_bf16_t;
 /* Device status bits, set by kernels and read by gdn_b200_device_status. */
 #define GDN_STATUS_WAIT_TIMEOUT 0x1u /* a bounded wait gave up; the kernel left early */
 #define GDN_STATUS_BAD_SLOT 0x2u     /* a slot index >= num_slots was skipped */
+#define GDN_STATUS_BAD_SEQLENS 0x4u  /* a sequence with invalid cu_seqlens bounds was skipped */
 
 /* Scale modes. */
 #define GDN_SCALE_REF240 0 /* the reference codec: scales saturate at 240 (0x77) */
@@ -160,6 +161,46 @@ typedef struct gdn_decode_params {
 } gdn_decode_params;
 
 GDN_API int gdn_decode(const gdn_decode_params* params, cudaStream_t stream);
+
+/* ---- chunked prefill (many tokens per sequence) -----------------------------
+ * The same recurrence as gdn_decode applied to every token of variable-length
+ * sequences, computed in chunks of 64 tokens in the WY/UT form.  Sequence n
+ * owns tokens [cu_seqlens[n], cu_seqlens[n+1]) of the packed q/k/v/g/beta/out
+ * rows.  Its initial state is the pool tile at slot_idx[n] when
+ * has_initial_state[n] != 0 (zero otherwise); its final state is quantised
+ * into that slot with a fresh global scale.  slot_idx == NULL (or a negative
+ * slot) runs the sequence from a zero state and keeps no final state.
+ * The reference has no prefill; its per-token Python loop
+ * (src/ops/qwen35_gdn_patch.py:98-116) is what this replaces. */
+typedef struct gdn_prefill_params {
+  int32_t num_seqs;       /* N */
+  int32_t num_k_heads;    /* HK */
+  int32_t num_v_heads;    /* HV, a multiple of HK */
+  int32_t head_dim;       /* d_k = d_v = 128 */
+  int64_t total_tokens;   /* rows of q, k, v, g, beta, out */
+  int64_t num_slots;      /* pool slots */
+  const gdn_bf16_t* q;    /* [T, HK, D], token stride q_stride */
+  const gdn_bf16_t* k;    /* [T, HK, D] */
+  const gdn_bf16_t* v;    /* [T, HV, D] */
+  int64_t q_stride;       /* elements between tokens; 0 = HK*D */
+  int64_t k_stride;       /* 0 = HK*D */
+  int64_t v_stride;       /* 0 = HV*D */
+  const float* g;         /* [T, HV] log decay */
+  const float* beta;      /* [T, HV] */
+  const int32_t* cu_seqlens;         /* [N + 1], non-decreasing, within [0, T] */
+  const int32_t* slot_idx;           /* [N] or NULL */
+  const uint8_t* has_initial_state;  /* [N] (bool) or NULL = all zero */
+  uint8_t* pool_codes;    /* [num_slots, HV, D, D/2] */
+  uint8_t* pool_scales;   /* [num_slots, HV, D, D/16] */
+  float* pool_gscale;     /* [num_slots, HV] */
+  gdn_bf16_t* out;        /* [T, HV, D] */
+  float q_scale;          /* <= 0 selects 1/sqrt(D) */
+  int32_t scale_mode;     /* GDN_SCALE_* */
+  float gscale_den;       /* <= 0 selects 6*saturation */
+  float* debug_y;         /* optional [N, HV, D, D]: fp32 quantiser inputs of the final states */
+} gdn_prefill_params;
+
+GDN_API int gdn_prefill(const gdn_prefill_params* params, cudaStream_t stream);
 
 /* ---- state pool ------------------------------------------------------------ */
 
