@@ -9,34 +9,36 @@
 //   A[r][s]  = beta_r (k_r . k_s) exp(G_r - G_s)            s < r   (else 0)
 //   T        = (I + A)^-1                                     (unit lower triangular)
 //   U        = T diag(beta) V,   W = T diag(beta gamma) K
-//   V_new    = U - W S                                        (the delta-rule w of every token)
-//   O        = q_scale (diag(gamma) Q S + P V_new),  P[r][s] = (q_r . k_s) exp(G_r - G_s), s <= r
+//   V_new    = U - W S = U - (T diag(beta gamma)) (K S)       (the delta-rule w of every token)
+//   O        = q_scale diag(gamma) Q S + P V_new,  P[r][s] = q_scale (q_r . k_s) exp(G_r - G_s), s <= r
 //   S_next   = gamma_{C-1} S + sum_s exp(G_{C-1} - G_s) k_s V_new_s^T
 // which equals the token-by-token recurrence exactly (in exact arithmetic).
 // The reference has no prefill (its serving loop calls the d x d update once
 // per token and sequence, src/ops/qwen35_gdn_patch.py:98-116).
 //
 // One CTA owns one (sequence, value head) at a time and walks its chunks in
-// order.  The state stays in tensor memory for the whole sequence, transposed
-// (TMEM lane = j over d_v, column = i over d_k), so that it is directly the A
-// operand of the two tf32 products that read it.  Per chunk:
-//   P1 (bf16)  [K; Q] K^T             -> K K^T and Q K^T in one M = 128 MMA
-//   SIMT       A, P, the blocked 16 x 16 triangular inverse T
-//   P2 (bf16)  U^T = V^T (T diag beta)^T
-//   P3 (bf16)  W^T = K^T (T diag(beta gamma))^T
-//   P4 (tf32)  U^T - S^T W^T          (accumulates onto U^T: V_new^T)
-//   P6a (tf32) S^T (q_scale diag(gamma) Q)^T
-//   P6b (tf32) + V_new^T P^T          -> O^T
-//   P7 (bf16)  S^T <- gamma S^T + V_new'^T K  (V_new' = V_new scaled by exp(G_{C-1} - G_s))
-// q, k, v rows arrive by 1-D bulk copies (one per 256-byte row) into a padded
-// staging buffer; the next chunk's copies are issued as soon as the current
-// chunk's operands are built, so they overlap the rest of the chunk.  At the
-// end of a sequence the state is requantised into its pool slot with the
-// reference block quantiser (tile_requant.cuh).  Every wait is bounded.
-//
-// All MMA operands use the no-swizzle K-major layout: 8-row x 16-byte core
-// matrices, 16-byte K chunks 128 bytes apart (LBO), 8-row groups SBO apart.
+// order.  The fp32 state stays in tensor memory for the whole sequence,
+// transposed (TMEM lane = j over d_v, column = i over d_k); a bf16 copy of it
+// in shared memory is the operand of the two products that read the state.
+// Per chunk, all on tcgen05 except the 64 x 64 triangular solve:
+//   P1  (bf16)  [K; Q] K^T            -> K K^T and Q K^T in one M = 128 MMA
+//   Y   (bf16)  S^T K^T,  O1 (bf16) S^T Q^T          (with P1: they need only S)
+//   SIMT        A, P, T = (I + A)^-1 in 16 x 16 blocks
+//   P2  (bf16)  U^T = V^T (T diag beta)^T
+//   P4  (tf32)  U^T += Y (-T diag(beta gamma))^T     -> V_new^T
+//   P6  (bf16)  O2 = V_new^T P^T
+//   P7  (bf16)  S^T <- gamma_{C-1} S^T + (V_new^T diag(exp(G_{C-1} - G))) K
+// q, k, v arrive by TMA tensor copies (128-byte swizzle) into a double-
+// buffered stage that the MMAs read in place: K and Q as K-major operands,
+// V and K as MN-major ones; the next-but-one chunk is loaded as soon as a
+// stage is released.  Outputs are staged in shared memory and stored as
+// 16-byte rows.  At the end of a sequence the state is requantised into its
+// pool slot with the reference block quantiser (tile_requant.cuh).  Every
+// wait is bounded.
 #include <cstdint>
+#include <mutex>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 
 #include "../common.cuh"
@@ -53,40 +55,41 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr uint32_t kCodeBytes = kD * kD / 2;
 constexpr uint32_t kScaleBytes = kD * kD / 16;
-constexpr uint32_t kRowBytes = kD * 2;  // one bf16 q/k/v row
-constexpr uint32_t kStgRow = 272;       // staged row pitch (16 bytes of padding against bank conflicts)
-constexpr uint32_t kStgBytes = kC * kStgRow;
 
-// Shared-memory map (bytes).  Regions are reused by phase; see each use.
-constexpr uint32_t kOffStgK = 0;
-constexpr uint32_t kOffStgQ = kStgBytes;
-constexpr uint32_t kOffStgV = 2 * kStgBytes;
-constexpr uint32_t kOffR1 = 3 * kStgBytes;      // [K;Q] bf16 -> solve scratch -> -W fp32
-constexpr uint32_t kSizeR1 = 39936;
-constexpr uint32_t kOffKt = kOffR1 + kSizeR1;   // K^T bf16 [d_k][C]
-constexpr uint32_t kOffR2 = kOffKt + 16384;     // V^T bf16, T', T'' -> V_new^T fp32 (or initial-state operands)
-constexpr uint32_t kOffR3 = kOffR2 + 32768;     // Q' fp32 -> V_new'^T bf16
-constexpr uint32_t kOffPm = kOffR3 + 32768;     // P fp32 [C][C]
-constexpr uint32_t kOffMisc = kOffPm + 16384;
-constexpr int kLd = 68;                         // solve scratch row pitch (floats)
-constexpr uint32_t kFPitch = 132;               // final-state transpose row pitch (floats)
-constexpr uint32_t kWnSbo = 4608;               // -W: 32 K chunks of 144 bytes per 8-row group
-constexpr uint32_t kWnLbo = 144;
+// One stage: six 64-row x 128-byte TMA boxes, 128-byte swizzled.
+constexpr uint32_t kBox = 8192;
+constexpr uint32_t kStK0 = 0, kStQ0 = kBox, kStK1 = 2 * kBox, kStQ1 = 3 * kBox, kStV0 = 4 * kBox, kStV1 = 5 * kBox;
+constexpr uint32_t kStage = 6 * kBox;
 
-static_assert(kOffR1 % 128 == 0 && kOffR2 % 128 == 0 && kOffR3 % 128 == 0 && kOffPm % 128 == 0, "alignment");
-static_assert(2 * 64 * kLd * 4 + 16 * kLd * 4 <= kSizeR1, "solve scratch fits R1");
-static_assert(8 * kWnSbo <= kSizeR1, "-W fits R1");
-static_assert(kOffR1 + 128 * kFPitch * 4 <= kOffR3, "final-state transpose fits R1..R2");
+// Shared-memory map (bytes).
+constexpr uint32_t kOffStage = 0;                    // 2 stages
+constexpr uint32_t kOffSB = 2 * kStage;              // bf16 state copy S^T [j][i]
+constexpr uint32_t kOffScr = kOffSB + 32768;         // solve scratch -> V_new^T operands -> output staging
+constexpr uint32_t kSizeScr = 39168;
+constexpr uint32_t kOffTpp = kOffScr + kSizeScr;     // T diag(beta), bf16 [r][s]
+constexpr uint32_t kOffNtp = kOffTpp + 8192;         // -T diag(beta gamma), fp32 [r][s]
+constexpr uint32_t kOffPm = kOffNtp + 16384;         // P, bf16 [r][s]
+constexpr uint32_t kOffMisc = kOffPm + 8192;
+constexpr int kLd = 68;                              // solve scratch row pitch (floats)
+constexpr uint32_t kOPitch = 272;                    // output staging row pitch (bytes)
+constexpr uint32_t kFPitch = 132;                    // final-state transpose row pitch (floats)
+
+static_assert(kOffSB % 1024 == 0 && kStage % 1024 == 0, "swizzled stages need 1024-byte alignment");
+static_assert(2 * 64 * kLd * 4 + 16 * kLd * 4 <= kSizeScr, "solve scratch");
+static_assert(2 * 16384 <= kSizeScr && 64 * kOPitch <= kSizeScr, "V_new operands / output staging");
+static_assert(kOffSB + 128 * kFPitch * 4 <= kOffTpp, "final-state transpose fits SB + scratch");
+static_assert(2 * kCodeBytes + 2 * kScaleBytes <= kSizeScr, "initial-state operands");
 
 // TMEM columns (512 allocated: one CTA per SM)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;     // 128: state S^T (lane j, column i)
+constexpr uint32_t kColS = 0;     // 128: state S^T (lane j, column i), fp32
 constexpr uint32_t kColKQ = 128;  // 64: [K K^T; Q K^T]
-constexpr uint32_t kColU = 192;   // 64: U^T, then V_new^T
-constexpr uint32_t kColW = 256;   // 64: W^T (lane i, column r)
-constexpr uint32_t kColO = 320;   // 64: O^T
-constexpr uint32_t kColSF = 384;  // 8: initial-state scale factors
-constexpr uint32_t kColOne = 392; // 8: unit scale factors
+constexpr uint32_t kColY = 192;   // 64: Y = S^T K^T
+constexpr uint32_t kColU = 256;   // 64: U^T, then V_new^T
+constexpr uint32_t kColO1 = 320;  // 64: S^T Q^T
+constexpr uint32_t kColO2 = 384;  // 64: V_new^T P^T
+constexpr uint32_t kColSF = 448;  // 8: initial-state scale factors
+constexpr uint32_t kColOne = 456; // 8: unit scale factors
 
 struct Misc {
   float gw[kC];    // warp-inclusive scans of g
@@ -94,9 +97,10 @@ struct Misc {
   float bet[kC];   // beta
   float bg[kC];    // beta * gamma
   float de[kC];    // exp(G_last - G)
+  float qg[kC];    // q_scale * gamma
   float inv_tab[256];
   float amax[kWarps];
-  uint64_t bar_stg, bar_mma;
+  uint64_t bar_stg[2], bar_mma;
   uint32_t tmem_base;
 };
 constexpr uint32_t kSmemBytes = kOffMisc + sizeof(Misc);
@@ -105,10 +109,6 @@ static_assert(kSmemBytes <= 232448, "shared memory");
 struct PrefillArgs {
   int32_t N, HK, HV, group, nitems;
   int64_t T, num_slots;
-  const __nv_bfloat16* q;
-  const __nv_bfloat16* k;
-  const __nv_bfloat16* v;
-  int64_t q_stride, k_stride, v_stride;
   const float* g;
   const float* beta;
   const int32_t* cu;
@@ -123,15 +123,13 @@ struct PrefillArgs {
   uint32_t* status;
 };
 
-// Byte offsets in the K-major no-swizzle layouts.
+// Byte offsets in the no-swizzle K-major layouts (16-byte K chunks 128 bytes
+// apart, 8-row groups sbo apart).
 __device__ __forceinline__ uint32_t kbf16(int row, int k, uint32_t sbo) {
   return (row & 7) * 16 + (k & 7) * 2 + (row >> 3) * sbo + (k >> 3) * 128;
 }
 __device__ __forceinline__ uint32_t kf32(int row, int k, uint32_t sbo) {
   return (row & 7) * 16 + (k & 3) * 4 + (row >> 3) * sbo + (k >> 2) * 128;
-}
-__device__ __forceinline__ uint32_t kwn(int r, int i) {
-  return (r & 7) * 16 + (i & 3) * 4 + (r >> 3) * kWnSbo + (i >> 2) * kWnLbo;
 }
 __device__ __forceinline__ int canon(int row, int byte) { return (byte & 15) + 16 * row + 2048 * (byte >> 4); }
 
@@ -179,35 +177,42 @@ __device__ __forceinline__ int chunk_len(const Cursor& c) {
   return rest < kC ? (int)rest : kC;
 }
 
-// Warp 0: queue the q, k, v rows of chunk c into the staging buffer.
-__device__ __forceinline__ void issue_chunk(const PrefillArgs& a, uint8_t* smem, uint64_t* bar, const Cursor& c,
-                                            int lane) {
-  const int64_t t0 = c.bos + c.chunk * kC;
-  const int len = chunk_len(c);
-  const int64_t hk = c.h / a.group;
-  if (lane == 0) mbar_arrive_expect_tx(bar, 3u * kRowBytes * (uint32_t)len);
-  __syncwarp();
-  for (int r = lane; r < len; r += 32) {
-    const int64_t t = t0 + r;
-    bulk_g2s(smem + kOffStgK + r * kStgRow, a.k + t * a.k_stride + hk * kD, kRowBytes, bar);
-    bulk_g2s(smem + kOffStgQ + r * kStgRow, a.q + t * a.q_stride + hk * kD, kRowBytes, bar);
-    bulk_g2s(smem + kOffStgV + r * kStgRow, a.v + t * a.v_stride + (int64_t)c.h * kD, kRowBytes, bar);
-  }
+// Thread 0: queue chunk c's k, q, v boxes into a stage.  Rows past the end of
+// the tensors arrive as zeros; rows past the end of the sequence are masked
+// by the consumers.
+__device__ __forceinline__ void issue_chunk(const PrefillArgs& a, uint8_t* stage, uint64_t* bar, const Cursor& c,
+                                            const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv) {
+  const int t0 = (int)(c.bos + c.chunk * kC);
+  const int hk = c.h / a.group;
+  mbar_arrive_expect_tx(bar, kStage);
+  tc::tma_load_3d(stage + kStK0, tk, 0, hk, t0, bar);
+  tc::tma_load_3d(stage + kStK1, tk, 64, hk, t0, bar);
+  tc::tma_load_3d(stage + kStQ0, tq, 0, hk, t0, bar);
+  tc::tma_load_3d(stage + kStQ1, tq, 64, hk, t0, bar);
+  tc::tma_load_3d(stage + kStV0, tv, 0, c.h, t0, bar);
+  tc::tma_load_3d(stage + kStV1, tv, 64, c.h, t0, bar);
 }
 
 // Threads 0..63: g and beta of token `r` of chunk c (0 past the chunk end).
 __device__ __forceinline__ void load_gb(const PrefillArgs& a, const Cursor& c, int r, float& gv, float& bv) {
   gv = 0.0f;
   bv = 0.0f;
-  if (r < chunk_len(c)) {
+  if (c.item < a.nitems && r < chunk_len(c)) {
     const int64_t idx = (c.bos + c.chunk * kC + r) * a.HV + c.h;
     gv = __ldg(a.g + idx);
     bv = __ldg(a.beta + idx);
   }
 }
 
+// K-major descriptor of rows [8 g, 8 g + 64 or 128) of a stage's K or Q, K step ks (16 elements).
+__device__ __forceinline__ uint64_t stage_kmajor(const uint8_t* stage, uint32_t box0, int ks) {
+  return tc::smem_desc_sw128(stage + box0 + (ks < 4 ? 0u : 2u * kBox) + 32u * (ks & 3), 16, 1024);
+}
+
 template <int kMode>
-__global__ void __launch_bounds__(kThreads, 1) gdn_prefill_kernel(const PrefillArgs a) {
+__global__ void __launch_bounds__(kThreads, 1)
+    gdn_prefill_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tm_q,
+                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
   extern __shared__ __align__(1024) uint8_t smem[];
   Misc& ms = *reinterpret_cast<Misc*>(smem + kOffMisc);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -215,26 +220,26 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_kernel(const PrefillA
   const int lrow = 32 * quad + lane;  // this thread's TMEM lane
   const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
 
-  uint8_t* const stg_k = smem + kOffStgK;
-  uint8_t* const stg_q = smem + kOffStgQ;
-  uint8_t* const stg_v = smem + kOffStgV;
-  uint8_t* const a1 = smem + kOffR1;
-  float* const Am = reinterpret_cast<float*>(smem + kOffR1);
+  // The swizzled stages need a 1024-byte aligned window.
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (tid == 0) atomicOr(a.status, kStatusWaitTimeout);
+    return;
+  }
+  uint8_t* const sb = smem + kOffSB;
+  float* const Am = reinterpret_cast<float*>(smem + kOffScr);
   float* const Tm = Am + 64 * kLd;
   float* const Xm = Tm + 64 * kLd;
-  uint8_t* const wn = smem + kOffR1;
-  uint8_t* const kt = smem + kOffKt;
-  uint8_t* const vt = smem + kOffR2;
-  uint8_t* const tp = smem + kOffR2 + 16384;   // T diag(beta gamma)
-  uint8_t* const tpp = smem + kOffR2 + 24576;  // T diag(beta)
-  uint8_t* const vn = smem + kOffR2;           // V_new^T fp32
-  uint8_t* const qp = smem + kOffR3;
-  uint8_t* const vnp = smem + kOffR3;          // V_new'^T bf16
+  uint8_t* const vn = smem + kOffScr;           // V_new^T bf16 [j][s]
+  uint8_t* const vnp = smem + kOffScr + 16384;  // V_new^T diag(exp(G_last - G)) bf16 [j][s]
+  uint8_t* const ost = smem + kOffScr;          // output rows bf16 [r][j]
+  uint8_t* const tpp = smem + kOffTpp;
+  uint8_t* const ntp = smem + kOffNtp;
   uint8_t* const pm = smem + kOffPm;
 
   ms.inv_tab[tid] = scale_inverse(scale_decode((uint32_t)tid, kMode));
   if (tid == 0) {
-    mbar_init(&ms.bar_stg, 1);
+    mbar_init(&ms.bar_stg[0], 1);
+    mbar_init(&ms.bar_stg[1], 1);
     mbar_init(&ms.bar_mma, 1);
     fence_mbar_init();
   }
@@ -243,25 +248,30 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_kernel(const PrefillA
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t T = ms.tmem_base;
-  const uint32_t id_bf16_64 = tc::idesc_bf16(128, 64);
-  const uint32_t id_bf16_128 = tc::idesc_bf16(128, 128);
-  const uint32_t id_tf32_64 = tc::idesc_tf32(128, 64);
+  const uint32_t id_kq = tc::idesc_bf16(128, 64);
+  const uint32_t id_u = tc::idesc_bf16(128, 64, true, false);
+  const uint32_t id_s = tc::idesc_bf16(128, 128, false, true);
+  const uint32_t id_tf = tc::idesc_tf32(128, 64);
   const uint32_t id_mx = tc::idesc_mxf4nvf4(128, 128);
 
   Cursor cur{(int32_t)blockIdx.x, 0, 0, 0, 0, 0};
   cursor_seek(a, cur, tid == 0);
-  Cursor ahead = cur;
-  float g_pre = 0.0f, b_pre = 0.0f;
-  bool stg_pending = false, mma_pending = false, failed = false;
-  uint32_t stg_par = 0, mma_par = 0;
-  if (cur.item < a.nitems) {
-    if (warp == 0) issue_chunk(a, smem, &ms.bar_stg, ahead, lane);
-    if (tid < kC) load_gb(a, ahead, tid, g_pre, b_pre);
-    stg_pending = true;
-    cursor_next(a, ahead, false);
+  Cursor ahead = cur;  // next chunk to load
+  uint32_t pending = 0, stg_par = 0;  // bit b: stage b has a load in flight / its barrier's phase parity
+  int use_buf = 0;
+  // Queue the first two chunks.
+  for (int b = 0; b < 2; ++b) {
+    if (ahead.item < a.nitems) {
+      if (tid == 0) issue_chunk(a, smem + kOffStage + b * kStage, &ms.bar_stg[b], ahead, &tm_q, &tm_k, &tm_v);
+      pending |= 1u << b;
+      cursor_next(a, ahead, false);
+    }
   }
+  float g_pre = 0.0f, b_pre = 0.0f;
+  if (tid < kC) load_gb(a, cur, tid, g_pre, b_pre);
 
-  // Issues the queued MMAs' commit (thread 0) and waits for them (all).
+  bool mma_pending = false, failed = false;
+  uint32_t mma_par = 0;
   auto mma_wait = [&]() -> bool {
     mma_pending = true;
     if (!mbar_wait_cta(&ms.bar_mma, mma_par)) return false;
@@ -278,12 +288,13 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_kernel(const PrefillA
   };
 
   int32_t slot = -1;
-  bool s_zero = true;  // the state in TMEM is not valid yet (zero initial state)
+  bool s_zero = true;  // the state is zero (not yet in TMEM / the bf16 copy)
   while (cur.item < a.nitems) {
     const int h = cur.h;
     const int64_t t0 = cur.bos + cur.chunk * kC;
     const int len = chunk_len(cur);
     const bool last = (cur.chunk + 1) * kC >= cur.len;
+    uint8_t* const stage = smem + kOffStage + use_buf * kStage;
 
     // ---- sequence start: slot and initial state ----
     if (cur.chunk == 0) {
@@ -299,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_kernel(const PrefillA
         // Decode the NVFP4 tile straight into TMEM with one block-scaled MMA
         // against the identity: D = I * S^T (lane j, column i).
         const int64_t pt = (int64_t)slot * a.HV + h;
-        uint8_t* const codes = smem + kOffR2;
+        uint8_t* const codes = smem + kOffScr;
         uint8_t* const ident = codes + kCodeBytes;
         uint8_t* const sf = ident + kCodeBytes;
         uint8_t* const sf_one = sf + kScaleBytes;
@@ -335,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_kernel(const PrefillA
           tc::commit(&ms.bar_mma);
         }
         if (!mma_wait()) { failed = true; break; }
+        // S *= gs in TMEM; the bf16 copy for the state products
         float sv[32];
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
@@ -344,16 +356,40 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_kernel(const PrefillA
 #pragma unroll
           for (int c = 0; c < 32; ++c) sv[c] *= gs;
           tc::st_32x32b_x32(ta, sv);
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            const int i = 64 * half + 32 * p + 8 * c8;
+            *reinterpret_cast<uint4*>(sb + kbf16(lrow, i, 2048)) =
+                make_uint4(pack_bf16(sv[8 * c8], sv[8 * c8 + 1]), pack_bf16(sv[8 * c8 + 2], sv[8 * c8 + 3]),
+                           pack_bf16(sv[8 * c8 + 4], sv[8 * c8 + 5]), pack_bf16(sv[8 * c8 + 6], sv[8 * c8 + 7]));
+          }
         }
         tc::st_wait();
-        tc::fence_before_sync();
+        sync_for_mma();
       }
     }
 
-    // ---- 0: staged rows -> MMA operands; g, beta -> cumulative decay ----
-    if (!mbar_wait_cta(&ms.bar_stg, stg_par)) { failed = true; break; }
-    stg_par ^= 1;
-    stg_pending = false;
+    // ---- 0: stage ready -> P1, Y, O1 on the tensor cores; decay prefix ----
+    if (!mbar_wait_cta(&ms.bar_stg[use_buf], (stg_par >> use_buf) & 1u)) { failed = true; break; }
+    stg_par ^= 1u << use_buf;
+    pending &= ~(1u << use_buf);
+    const bool s0 = s_zero;
+    if (tid == 0) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t dk = stage_kmajor(stage, kStK0, ks);
+        tc::mma_bf16_ss(T + kColKQ, dk, dk, id_kq, ks > 0);  // [K; Q] K^T: rows 64..127 are Q's box
+      }
+      if (!s0) {
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint64_t ds = tc::smem_desc(sb + 256 * ks, 128, 2048);
+          tc::mma_bf16_ss(T + kColY, ds, stage_kmajor(stage, kStK0, ks), id_kq, ks > 0);
+          tc::mma_bf16_ss(T + kColO1, ds, stage_kmajor(stage, kStQ0, ks), id_kq, ks > 0);
+        }
+      }
+      tc::commit(&ms.bar_mma);
+    }
     const float gv = g_pre, bv = b_pre;
     if (tid < kC) {
       float s = gv;
@@ -363,122 +399,58 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_kernel(const PrefillA
         if (lane >= o) s += y;
       }
       ms.gw[tid] = s;
-      ms.bet[tid] = bv;
+      // prefetch g, beta of the next chunk
+      Cursor nx = cur;
+      cursor_next(a, nx, false);
+      load_gb(a, nx, tid, g_pre, b_pre);
     }
-    // [K; Q] rows (bf16, 128 x 128): thread moves 16-byte chunks; rows past the chunk end are zero.
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int e = tid + kThreads * it;
-      const int row_lo = e & 7, c = (e >> 3) & 15, row_hi = e >> 7;
-      const int row = row_lo + 8 * row_hi;
-      const int r = row & 63;
-      uint4 val = make_uint4(0u, 0u, 0u, 0u);
-      if (r < len) val = *reinterpret_cast<const uint4*>((row < 64 ? stg_k : stg_q) + r * kStgRow + 16 * c);
-      *reinterpret_cast<uint4*>(a1 + row_lo * 16 + row_hi * 2048 + c * 128) = val;
-    }
-    tc::fence_smem_to_async();
     __syncthreads();
-    if (tid == 0) {
-      // P1: [K K^T; Q K^T] = [K; Q] K^T  (M = 128, N = 64, K = 128)
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint64_t d = tc::smem_desc(a1 + 256 * ks, 128, 2048);
-        tc::mma_bf16_ss(T + kColKQ, d, d, id_bf16_64, ks > 0);
-      }
-      tc::commit(&ms.bar_mma);
-    }
     if (tid < kC) {
       const float G = ms.gw[tid] + (tid >= 32 ? ms.gw[31] : 0.0f);
       const float Glast = ms.gw[63] + ms.gw[31];
       const float gm = __expf(G);
       ms.G[tid] = G;
+      ms.bet[tid] = bv;
       ms.bg[tid] = bv * gm;
       ms.de[tid] = __expf(Glast - G);
+      ms.qg[tid] = a.q_scale * gm;
     }
-    // K^T, V^T (bf16 [d][C]): thread gathers 8 tokens of one column.
-#pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      const int e = tid + kThreads * it;
-      const int i = e & 127, s8 = e >> 7;
-      uint32_t wk[4], wv[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int s = 8 * s8 + 2 * t;
-        uint32_t k0 = 0, k1 = 0, v0 = 0, v1 = 0;
-        if (s < len) {
-          k0 = reinterpret_cast<const uint16_t*>(stg_k + s * kStgRow)[i];
-          v0 = reinterpret_cast<const uint16_t*>(stg_v + s * kStgRow)[i];
-        }
-        if (s + 1 < len) {
-          k1 = reinterpret_cast<const uint16_t*>(stg_k + (s + 1) * kStgRow)[i];
-          v1 = reinterpret_cast<const uint16_t*>(stg_v + (s + 1) * kStgRow)[i];
-        }
-        wk[t] = k0 | (k1 << 16);
-        wv[t] = v0 | (v1 << 16);
-      }
-      const uint32_t off = (i & 7) * 16 + (i >> 3) * 1024 + s8 * 128;
-      *reinterpret_cast<uint4*>(kt + off) = make_uint4(wk[0], wk[1], wk[2], wk[3]);
-      *reinterpret_cast<uint4*>(vt + off) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-    }
-    __syncthreads();  // G, bg, de published
-    const float Glast = ms.G[kC - 1];
-    // Q' = q_scale gamma_r q_r (fp32 [C][d_k])
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int e = tid + kThreads * it;
-      const int r_lo = e & 7, i4 = (e >> 3) & 31, r_hi = e >> 8;
-      const int r = r_lo + 8 * r_hi;
-      float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      if (r < len) {
-        const float sc = a.q_scale * __expf(ms.G[r]);
-        const uint2 raw = *reinterpret_cast<const uint2*>(stg_q + r * kStgRow + 8 * i4);
-        const __nv_bfloat162 q01 = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-        const __nv_bfloat162 q23 = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-        o = make_float4(sc * __low2float(q01), sc * __high2float(q01), sc * __low2float(q23), sc * __high2float(q23));
-      }
-      *reinterpret_cast<float4*>(qp + r_lo * 16 + r_hi * 4096 + i4 * 128) = o;
-    }
-    tc::fence_smem_to_async();
-    __syncthreads();  // staging consumed: queue the next chunk
-    if (ahead.item < a.nitems) {
-      if (warp == 0) issue_chunk(a, smem, &ms.bar_stg, ahead, lane);
-      if (tid < kC) load_gb(a, ahead, tid, g_pre, b_pre);
-      stg_pending = true;
-      cursor_next(a, ahead, false);
-    }
+    if (!mma_wait()) { failed = true; break; }  // also publishes G, bet, bg, de, qg
 
     // ---- 1: A (strictly lower, for the solve) and P (lower incl. diagonal) ----
-    if (!mma_wait()) { failed = true; break; }
     {
       float vals[32];
       tc::ld_32x32b_x32(T + lane_base + kColKQ + 32 * half, vals);
       tc::ld_wait();
-      const int sb = 32 * half;
+      const int sb0 = 32 * half;
       if (quad < 2) {
         const int r = lrow;
         const float Gr = ms.G[r], br = ms.bet[r];
 #pragma unroll
         for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 Gs = *reinterpret_cast<const float4*>(ms.G + sb0 + 4 * c4);
+          const float gsv[4] = {Gs.x, Gs.y, Gs.z, Gs.w};
           float o[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int s = sb + 4 * c4 + e;
-            o[e] = (s < r) ? br * vals[4 * c4 + e] * __expf(Gr - ms.G[s]) : 0.0f;
+            const int s = sb0 + 4 * c4 + e;
+            o[e] = (s < r) ? br * vals[4 * c4 + e] * __expf(Gr - gsv[e]) : 0.0f;
           }
-          *reinterpret_cast<float4*>(Am + r * kLd + sb + 4 * c4) = make_float4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<float4*>(Am + r * kLd + sb0 + 4 * c4) = make_float4(o[0], o[1], o[2], o[3]);
         }
       } else {
         const int r = lrow - 64;
         const float Gr = ms.G[r];
 #pragma unroll
-        for (int c4 = 0; c4 < 8; ++c4) {
-          float o[4];
+        for (int c8 = 0; c8 < 4; ++c8) {
+          float o[8];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int s = sb + 4 * c4 + e;
-            o[e] = (s <= r) ? a.q_scale * vals[4 * c4 + e] * __expf(Gr - ms.G[s]) : 0.0f;
+          for (int e = 0; e < 8; ++e) {
+            const int s = sb0 + 8 * c8 + e;
+            o[e] = (s <= r) ? a.q_scale * vals[8 * c8 + e] * __expf(Gr - ms.G[s]) : 0.0f;
           }
-          *reinterpret_cast<float4*>(pm + kf32(r, sb + 4 * c4, 2048)) = make_float4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(pm + kbf16(r, sb0 + 8 * c8, 1024)) =
+              make_uint4(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]), pack_bf16(o[4], o[5]), pack_bf16(o[6], o[7]));
         }
       }
     }
@@ -492,11 +464,18 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_kernel(const PrefillA
       float x[16];
 #pragma unroll
       for (int r = 0; r < 16; ++r) {
-        const float* arow = Am + (16 * b + r) * kLd + 16 * b;
-        float acc = 0.0f;
+        const float4* arow = reinterpret_cast<const float4*>(Am + (16 * b + r) * kLd + 16 * b);
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int s = 0; s < r; ++s) acc = fmaf(arow[s], x[s], acc);
-        x[r] = (r < c) ? 0.0f : (r == c ? 1.0f : -acc);
+        for (int s4 = 0; s4 < (r + 3) / 4; ++s4) {
+          const float4 av = arow[s4];
+          const float aa[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (4 * s4 + e < r) acc[e] = fmaf(aa[e], x[4 * s4 + e], acc[e]);
+        }
+        const float sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+        x[r] = (r < c) ? 0.0f : (r == c ? 1.0f : -sum);
       }
 #pragma unroll
       for (int r = 0; r < 16; ++r) Tm[(16 * b + r) * kLd + 16 * b + c] = x[r];
@@ -517,107 +496,92 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_kernel(const PrefillA
 #pragma unroll
       for (int m = 0; m < ib; ++m) {
         const int j = jj + 16 * m;
-        const float* arow = Am + (16 * ib + r) * kLd;
-        float acc = 0.0f;
+        const float4* arow = reinterpret_cast<const float4*>(Am + (16 * ib + r) * kLd);
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int kk = 16 * m; kk < 16 * ib; ++kk) acc = fmaf(arow[kk], Tm[kk * kLd + j], acc);
-        Xm[r * kLd + j] = acc;
+        for (int k4 = 4 * m; k4 < 4 * ib; ++k4) {
+          const float4 av = arow[k4];
+          acc[0] = fmaf(av.x, Tm[(4 * k4 + 0) * kLd + j], acc[0]);
+          acc[1] = fmaf(av.y, Tm[(4 * k4 + 1) * kLd + j], acc[1]);
+          acc[2] = fmaf(av.z, Tm[(4 * k4 + 2) * kLd + j], acc[2]);
+          acc[3] = fmaf(av.w, Tm[(4 * k4 + 3) * kLd + j], acc[3]);
+        }
+        Xm[r * kLd + j] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
       }
       __syncthreads();
       // T[block row ib][0 : 16 ib] = -D_ib X
 #pragma unroll
       for (int m = 0; m < ib; ++m) {
         const int j = jj + 16 * m;
-        const float* drow = Tm + (16 * ib + r) * kLd + 16 * ib;
-        float acc = 0.0f;
+        const float4* drow = reinterpret_cast<const float4*>(Tm + (16 * ib + r) * kLd + 16 * ib);
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int t = 0; t < 16; ++t) acc = fmaf(drow[t], Xm[t * kLd + j], acc);
-        Tm[(16 * ib + r) * kLd + j] = -acc;
+        for (int t4 = 0; t4 < 4; ++t4) {
+          const float4 dv = drow[t4];
+          acc[0] = fmaf(dv.x, Xm[(4 * t4 + 0) * kLd + j], acc[0]);
+          acc[1] = fmaf(dv.y, Xm[(4 * t4 + 1) * kLd + j], acc[1]);
+          acc[2] = fmaf(dv.z, Xm[(4 * t4 + 2) * kLd + j], acc[2]);
+          acc[3] = fmaf(dv.w, Xm[(4 * t4 + 3) * kLd + j], acc[3]);
+        }
+        Tm[(16 * ib + r) * kLd + j] = -((acc[0] + acc[1]) + (acc[2] + acc[3]));
       }
       __syncthreads();
     }
-    // T' = T diag(beta gamma), T'' = T diag(beta) as bf16 B operands ([r][s], K = s)
+    // T diag(beta) as bf16, -T diag(beta gamma) as fp32: B operands ([r][s], K = s)
 #pragma unroll
     for (int sp = 0; sp < 2; ++sp) {
       const int r = tid & 63, s8 = 2 * (tid >> 6) + sp;
       const float4 t0v = *reinterpret_cast<const float4*>(Tm + r * kLd + 8 * s8);
       const float4 t1v = *reinterpret_cast<const float4*>(Tm + r * kLd + 8 * s8 + 4);
       const float tv[8] = {t0v.x, t0v.y, t0v.z, t0v.w, t1v.x, t1v.y, t1v.z, t1v.w};
-      uint32_t pa[4], pb[4];
+      uint32_t pb[4];
+      float nt[8];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int s = 8 * s8 + 2 * e;
-        pa[e] = pack_bf16(tv[2 * e] * ms.bg[s], tv[2 * e + 1] * ms.bg[s + 1]);
-        pb[e] = pack_bf16(tv[2 * e] * ms.bet[s], tv[2 * e + 1] * ms.bet[s + 1]);
-      }
-      const uint32_t off = kbf16(r, 8 * s8, 1024);
-      *reinterpret_cast<uint4*>(tp + off) = make_uint4(pa[0], pa[1], pa[2], pa[3]);
-      *reinterpret_cast<uint4*>(tpp + off) = make_uint4(pb[0], pb[1], pb[2], pb[3]);
+      for (int e = 0; e < 8; ++e) nt[e] = -tv[e] * ms.bg[8 * s8 + e];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        pb[e] = pack_bf16(tv[2 * e] * ms.bet[8 * s8 + 2 * e], tv[2 * e + 1] * ms.bet[8 * s8 + 2 * e + 1]);
+      *reinterpret_cast<uint4*>(tpp + kbf16(r, 8 * s8, 1024)) = make_uint4(pb[0], pb[1], pb[2], pb[3]);
+      *reinterpret_cast<float4*>(ntp + kf32(r, 8 * s8, 2048)) = make_float4(nt[0], nt[1], nt[2], nt[3]);
+      *reinterpret_cast<float4*>(ntp + kf32(r, 8 * s8 + 4, 2048)) = make_float4(nt[4], nt[5], nt[6], nt[7]);
     }
     sync_for_mma();
-    const bool s0 = s_zero;
     if (tid == 0) {
-      // P2: U^T = V^T T''^T  (M = d_v, N = C, K = C)
+      // P2: U^T = V^T T''^T  (A = V as MN-major, M = d_v, N = C, K = C)
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        tc::mma_bf16_ss(T + kColU, tc::smem_desc(vt + 256 * ks, 128, 1024), tc::smem_desc(tpp + 256 * ks, 128, 1024),
-                        id_bf16_64, ks > 0);
+        tc::mma_bf16_ss(T + kColU, tc::smem_desc_sw128(stage + kStV0 + 2048 * ks, kBox, 1024),
+                        tc::smem_desc(tpp + 256 * ks, 128, 1024), id_u, ks > 0);
       if (!s0) {
-        // P3: W^T = K^T T'^T  (M = d_k)
+        // P4: V_new^T = U^T + Y (-T')^T  (tf32, A = Y from TMEM)
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16_ss(T + kColW, tc::smem_desc(kt + 256 * ks, 128, 1024),
-                          tc::smem_desc(tp + 256 * ks, 128, 1024), id_bf16_64, ks > 0);
+        for (int ks = 0; ks < 8; ++ks)
+          tc::mma_tf32_ts(T + kColU, T + kColY + 8 * ks, tc::smem_desc(ntp + 256 * ks, 128, 2048), id_tf, 1);
       }
       tc::commit(&ms.bar_mma);
     }
     if (!mma_wait()) { failed = true; break; }
 
-    // ---- 3: V_new^T = U^T - S^T W^T and O^T = S^T Q'^T (skipped while S = 0) ----
-    if (!s0) {
-      float vals[32];
-      tc::ld_32x32b_x32(T + lane_base + kColW + 32 * half, vals);
-      tc::ld_wait();
-      const int i = lrow;
-#pragma unroll
-      for (int c = 0; c < 32; ++c) *reinterpret_cast<float*>(wn + kwn(32 * half + c, i)) = -vals[c];
-      sync_for_mma();
-      if (tid == 0) {
-#pragma unroll
-        for (int ks = 0; ks < 16; ++ks)
-          tc::mma_tf32_ts(T + kColU, T + kColS + 8 * ks, tc::smem_desc(wn + 2 * kWnLbo * ks, kWnLbo, kWnSbo),
-                          id_tf32_64, 1);
-#pragma unroll
-        for (int ks = 0; ks < 16; ++ks)
-          tc::mma_tf32_ts(T + kColO, T + kColS + 8 * ks, tc::smem_desc(qp + 256 * ks, 128, 4096), id_tf32_64,
-                          ks > 0);
-        tc::commit(&ms.bar_mma);
-      }
-      if (!mma_wait()) { failed = true; break; }
-    }
-
-    // ---- 4: V_new^T -> operands; decay the state ----
+    // ---- 3: V_new^T -> operands; decay the state ----
     {
       float vals[32];
       tc::ld_32x32b_x32(T + lane_base + kColU + 32 * half, vals);
       tc::ld_wait();
-      const int j = lrow, sb = 32 * half;
-#pragma unroll
-      for (int c4 = 0; c4 < 8; ++c4)
-        *reinterpret_cast<float4*>(vn + kf32(j, sb + 4 * c4, 2048)) =
-            make_float4(vals[4 * c4], vals[4 * c4 + 1], vals[4 * c4 + 2], vals[4 * c4 + 3]);
+      const int j = lrow, sb0 = 32 * half;
 #pragma unroll
       for (int c8 = 0; c8 < 4; ++c8) {
-        uint32_t w[4];
+        uint32_t w[4], wd[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int c = 8 * c8 + 2 * e;
-          w[e] = pack_bf16(vals[c] * ms.de[sb + c], vals[c + 1] * ms.de[sb + c + 1]);
+          w[e] = pack_bf16(vals[c], vals[c + 1]);
+          wd[e] = pack_bf16(vals[c] * ms.de[sb0 + c], vals[c + 1] * ms.de[sb0 + c + 1]);
         }
-        *reinterpret_cast<uint4*>(vnp + kbf16(j, sb + 8 * c8, 1024)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(vn + kbf16(j, sb0 + 8 * c8, 1024)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(vnp + kbf16(j, sb0 + 8 * c8, 1024)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
       }
       if (!s0) {
-        const float gC = __expf(Glast);
+        const float gC = __expf(ms.G[kC - 1]);
         float sv[32];
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
@@ -633,37 +597,76 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_kernel(const PrefillA
     }
     sync_for_mma();
     if (tid == 0) {
-      // P6b: O^T += V_new^T P^T  (M = d_v, N = C, K = C)
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks)
-        tc::mma_tf32_ss(T + kColO, tc::smem_desc(vn + 256 * ks, 128, 2048), tc::smem_desc(pm + 256 * ks, 128, 2048),
-                        id_tf32_64, !s0 || ks > 0);
-      // P7: S^T += V_new'^T K  (M = d_v, N = d_k, K = C)
+      // P6: O2 = V_new^T P^T  (M = d_v, N = C, K = C)
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
-        tc::mma_bf16_ss(T + kColS, tc::smem_desc(vnp + 256 * ks, 128, 1024), tc::smem_desc(kt + 256 * ks, 128, 1024),
-                        id_bf16_128, !s0 || ks > 0);
+        tc::mma_bf16_ss(T + kColO2, tc::smem_desc(vn + 256 * ks, 128, 1024), tc::smem_desc(pm + 256 * ks, 128, 1024),
+                        id_kq, ks > 0);
+      // P7: S^T += V_new'^T K  (B = K as MN-major, N = d_k)
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        tc::mma_bf16_ss(T + kColS, tc::smem_desc(vnp + 256 * ks, 128, 1024),
+                        tc::smem_desc_sw128(stage + kStK0 + 2048 * ks, 2 * kBox, 1024), id_s, !s0 || ks > 0);
       tc::commit(&ms.bar_mma);
     }
     if (!mma_wait()) { failed = true; break; }
     s_zero = false;
+    // The stage is free: queue the next chunk to load into it.
+    if (ahead.item < a.nitems) {
+      if (tid == 0) issue_chunk(a, stage, &ms.bar_stg[use_buf], ahead, &tm_q, &tm_k, &tm_v);
+      pending |= 1u << use_buf;
+      cursor_next(a, ahead, false);
+    }
+    use_buf ^= 1;
 
-    // ---- 5: O^T -> out (bf16 [T, HV, d_v]) ----
+    // ---- 4: outputs O = diag(q_scale gamma) O1 + O2 -> bf16 rows ----
     {
-      float vals[32];
-      tc::ld_32x32b_x32(T + lane_base + kColO + 32 * half, vals);
+      float v2[32], v1[32];
+      tc::ld_32x32b_x32(T + lane_base + kColO2 + 32 * half, v2);
+      if (!s0) tc::ld_32x32b_x32(T + lane_base + kColO1 + 32 * half, v1);
       tc::ld_wait();
-      const int64_t row_stride = (int64_t)a.HV * kD;
-      __nv_bfloat16* ob = a.out + (t0 + 32 * half) * row_stride + (int64_t)h * kD + lrow;
+      const int j = lrow;
 #pragma unroll
-      for (int c = 0; c < 32; ++c)
-        if (32 * half + c < len) ob[c * row_stride] = __float2bfloat16_rn(vals[c]);
+      for (int c = 0; c < 32; ++c) {
+        const int r = 32 * half + c;
+        const float o = s0 ? v2[c] : fmaf(ms.qg[r], v1[c], v2[c]);
+        *reinterpret_cast<__nv_bfloat16*>(ost + r * kOPitch + 2 * j) = __float2bfloat16_rn(o);
+      }
     }
     tc::fence_before_sync();
+    __syncthreads();
+    {
+      const int64_t row_stride = (int64_t)a.HV * kD;
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int e = tid + kThreads * it;
+        const int r = e >> 4, c16 = e & 15;
+        if (r < len)
+          *reinterpret_cast<uint4*>(a.out + (t0 + r) * row_stride + (int64_t)h * kD + 8 * c16) =
+              *reinterpret_cast<const uint4*>(ost + r * kOPitch + 16 * c16);
+      }
+    }
 
-    // ---- sequence end: requantise the state into its slot ----
-    if (last) {
-      float* F = reinterpret_cast<float*>(smem + kOffR1);
+    if (!last) {
+      // bf16 copy of the updated state for the next chunk's state products
+      float sv[32];
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        tc::ld_32x32b_x32(T + lane_base + kColS + 64 * half + 32 * p, sv);
+        tc::ld_wait();
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          const int i = 64 * half + 32 * p + 8 * c8;
+          *reinterpret_cast<uint4*>(sb + kbf16(lrow, i, 2048)) =
+              make_uint4(pack_bf16(sv[8 * c8], sv[8 * c8 + 1]), pack_bf16(sv[8 * c8 + 2], sv[8 * c8 + 3]),
+                         pack_bf16(sv[8 * c8 + 4], sv[8 * c8 + 5]), pack_bf16(sv[8 * c8 + 6], sv[8 * c8 + 7]));
+        }
+      }
+      sync_for_mma();  // also: output staging read before the next chunk reuses it
+    } else {
+      // ---- sequence end: requantise the state into its slot ----
+      float* F = reinterpret_cast<float*>(smem + kOffSB);
+      __syncthreads();  // output staging read (it overlaps F)
       float sv[32];
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
@@ -714,13 +717,42 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_prefill_kernel(const PrefillA
     // Report, then give the copies and MMAs still queued a bounded chance to
     // finish before the shared and tensor memory are released.
     atomicOr(a.status, kStatusWaitTimeout);
-    if (stg_pending) mbar_wait_bounded(&ms.bar_stg, stg_par, kWaitTimeoutNs / 4);
+    for (int b = 0; b < 2; ++b)
+      if ((pending >> b) & 1u) mbar_wait_bounded(&ms.bar_stg[b], (stg_par >> b) & 1u, kWaitTimeoutNs / 4);
     if (mma_pending) mbar_wait_bounded(&ms.bar_mma, mma_par, kWaitTimeoutNs / 4);
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   if (warp == 0) tc::tmem_dealloc(T, kTmemCols);
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Tensor map over rows [T][heads][128] bf16 (token stride in elements): boxes of
+// 64 tokens x 64 features of one head, 128-byte swizzled, zero fill past T.
+bool make_row_map(CUtensorMap* m, const void* base, int64_t heads, int64_t T, int64_t token_stride) {
+  const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)heads, (cuuint64_t)T};
+  const cuuint64_t strides[2] = {(cuuint64_t)kD * 2, (cuuint64_t)token_stride * 2};
+  const cuuint32_t box[3] = {64, 1, 64};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -741,6 +773,16 @@ extern "C" int gdn_prefill(const gdn_prefill_params* p, cudaStream_t stream) {
   if (p->total_tokens > INT32_MAX) return GDN_ERR_UNSUPPORTED;  // cu_seqlens are int32
   const int64_t nitems = (int64_t)p->num_seqs * p->num_v_heads;
   if (nitems > INT32_MAX / 2) return GDN_ERR_UNSUPPORTED;
+  const int64_t q_stride = p->q_stride ? p->q_stride : (int64_t)p->num_k_heads * kD;
+  const int64_t k_stride = p->k_stride ? p->k_stride : (int64_t)p->num_k_heads * kD;
+  const int64_t v_stride = p->v_stride ? p->v_stride : (int64_t)p->num_v_heads * kD;
+  if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->out) ||
+      (q_stride | k_stride | v_stride) % 8 || (p->debug_y && !aligned16(p->debug_y)) ||
+      (p->slot_idx && (!aligned16(p->pool_codes) || !aligned16(p->pool_scales))))
+    return GDN_ERR_ALIGN;
+  if (q_stride < (int64_t)p->num_k_heads * kD || k_stride < (int64_t)p->num_k_heads * kD ||
+      v_stride < (int64_t)p->num_v_heads * kD)
+    return GDN_ERR_ARGS;
   PrefillArgs a;
   a.N = p->num_seqs;
   a.HK = p->num_k_heads;
@@ -749,16 +791,6 @@ extern "C" int gdn_prefill(const gdn_prefill_params* p, cudaStream_t stream) {
   a.nitems = (int32_t)nitems;
   a.T = p->total_tokens;
   a.num_slots = p->num_slots;
-  a.q = p->q;
-  a.k = p->k;
-  a.v = p->v;
-  a.q_stride = p->q_stride ? p->q_stride : (int64_t)p->num_k_heads * kD;
-  a.k_stride = p->k_stride ? p->k_stride : (int64_t)p->num_k_heads * kD;
-  a.v_stride = p->v_stride ? p->v_stride : (int64_t)p->num_v_heads * kD;
-  if (!aligned16(a.q) || !aligned16(a.k) || !aligned16(a.v) || !aligned16(p->out) ||
-      (a.q_stride | a.k_stride | a.v_stride) % 8 || (p->debug_y && !aligned16(p->debug_y)) ||
-      (p->slot_idx && (!aligned16(p->pool_codes) || !aligned16(p->pool_scales))))
-    return GDN_ERR_ALIGN;
   a.g = p->g;
   a.beta = p->beta;
   a.cu = p->cu_seqlens;
@@ -774,6 +806,11 @@ extern "C" int gdn_prefill(const gdn_prefill_params* p, cudaStream_t stream) {
   a.debug_y = p->debug_y;
   a.status = device_status_ptr();
   if (!a.status) return GDN_ERR_CUDA;
+  CUtensorMap tq, tk, tv;
+  if (!make_row_map(&tq, p->q, p->num_k_heads, p->total_tokens, q_stride) ||
+      !make_row_map(&tk, p->k, p->num_k_heads, p->total_tokens, k_stride) ||
+      !make_row_map(&tv, p->v, p->num_v_heads, p->total_tokens, v_stride))
+    return GDN_ERR_CUDA;
 
   const int smem = (int)kSmemBytes;
   const int64_t max_ctas = sm_count();
@@ -791,8 +828,8 @@ extern "C" int gdn_prefill(const gdn_prefill_params* p, cudaStream_t stream) {
     attr_set[mi][dev] = true;
   }
   if (mi == 0)
-    gdn_prefill_kernel<kScaleRef240><<<grid, kThreads, smem, stream>>>(a);
+    gdn_prefill_kernel<kScaleRef240><<<grid, kThreads, smem, stream>>>(a, tq, tk, tv);
   else
-    gdn_prefill_kernel<kScaleFn448><<<grid, kThreads, smem, stream>>>(a);
+    gdn_prefill_kernel<kScaleFn448><<<grid, kThreads, smem, stream>>>(a, tq, tk, tv);
   return launch_status();
 }

@@ -35,6 +35,17 @@ __device__ __forceinline__ uint64_t smem_desc(const void* base, uint32_t lbo_byt
   return d;
 }
 
+// As smem_desc, for the 128-byte swizzled layout that TMA writes with
+// CU_TENSOR_MAP_SWIZZLE_128B (8 rows x 128 bytes per 1024-byte atom, 16-byte
+// chunk c of row r stored at chunk c ^ (r % 8); atoms 1024-byte aligned).
+//   K-major:  SBO = distance between 8-row groups; LBO unused (16).  Advancing
+//             K within the atom moves the start address by the K bytes.
+//   MN-major: LBO = distance between 64-element MN atoms; SBO = distance
+//             between groups of 8 K rows.
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* base, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  return smem_desc(base, lbo_bytes, sbo_bytes) | (2ull << 61);
+}
+
 // Instruction descriptor, block-scaled E2M1 x E2M1 (kind::mxf4nvf4), UE4M3
 // scale factors, fp32 accumulate, K-major A and B, K = 64 per instruction.
 __host__ __device__ constexpr uint32_t idesc_mxf4nvf4(int M, int N) {
@@ -56,9 +67,10 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
 }
 
 // Instruction descriptor, kind::f16 with bf16 operands, fp32 accumulate,
-// K-major A and B, K = 16 per instruction.
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// K = 16 per instruction; A and B K-major unless a_mn / b_mn select MN-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn = false, bool b_mn = false) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // ---- TMEM allocation (one warp) ----------------------------------------------------
