@@ -52,6 +52,7 @@ UNIT = "tokens/s"
 B, HK, HV, D = 256, 16, 32, 128
 NUM_SLOTS = 256
 N_POOLS = 6
+SCALE_MODE = 1  # E4M3 scales (saturate at 448), global scale amax / (6 * 448)
 BYTES_PER_TOKEN = 614_916  # 32 x (8192 + 1024) x 2 + 32 x 4 x 2 + 24,576 + 256 + 4
 WORKLOAD = "decode_b256_hk16_hv32_d128_pool256"
 
@@ -59,7 +60,7 @@ WORKLOAD = "decode_b256_hk16_hv32_d128_pool256"
 def _config(n_gpus: int) -> dict:
     return {"workload": WORKLOAD, "batch_per_gpu": B, "num_k_heads": HK, "num_v_heads": HV, "head_dim": D,
             "pool_slots": NUM_SLOTS, "state_format": "nvfp4 e2m1 + ue4m3/16 + fp32 per-head global scale",
-            "scale_mode": "ref240", "parallelism": f"dp{n_gpus} (sequences sharded, no collective)",
+            "scale_mode": "fn448, gs = amax/(6*448)", "parallelism": f"dp{n_gpus} (sequences sharded, no collective)",
             "l2": f"inputs rotate over {N_POOLS} pools + input sets (453 MB > 126 MB L2)"}
 
 
@@ -167,11 +168,13 @@ def cpu_decode_sample(seconds: float, threads: int | None = None) -> dict:
     from oracle import bindings as ob
 
     lib, kind = ob.cpu_baseline(prefer_reference=True)
+    # the reference host codec saturates scales at 240: pair it with gs = amax/(6*240)
+    mode, gden = (0, 6.0 * 240.0) if kind == "reference" else (SCALE_MODE, 6.0 * 448.0)
     nthreads = threads or lib.cpu_max_threads()
     sample_seqs = 16
     x = workloads.decode_steps(sample_seqs, 1, HK, HV, D, seed=0)
     states = workloads.initial_states(sample_seqs, HV, D, seed=1).numpy()
-    codes, scales, gs, _ = ob.quantise_tiles(states.reshape(-1), D * D, 0)
+    codes, scales, gs, _ = ob.quantise_tiles(states.reshape(-1), D * D, mode, gden)
     codes = codes.reshape(sample_seqs, HV, D, D // 2).copy()
     scales = scales.reshape(sample_seqs, HV, D, D // 16).copy()
     gs = gs.reshape(sample_seqs, HV).copy()
@@ -188,7 +191,7 @@ def cpu_decode_sample(seconds: float, threads: int | None = None) -> dict:
     t0 = time.perf_counter()
     while True:
         lib.cpu_gdn_decode(sample_seqs, HK, HV, D, P(q), P(k), P(v), P(g), P(be), P(slot), P(codes), P(scales),
-                           P(gs), P(o), 1.0 / math.sqrt(D), 0, 1440.0, 0, sample_seqs * HV, nthreads)
+                           P(gs), P(o), 1.0 / math.sqrt(D), mode, gden, 0, sample_seqs * HV, nthreads)
         calls += 1
         el = time.perf_counter() - t0
         if el >= seconds:
@@ -222,7 +225,7 @@ def run_ours(args, dist, rank, world, local) -> dict | None:
     gen = torch.Generator(device=dev)
     for i in range(N_POOLS):
         gen.manual_seed(1000 * rank + i)
-        p = NVFP4StatePool.zeros(NUM_SLOTS, HV, D, dev)
+        p = NVFP4StatePool.zeros(NUM_SLOTS, HV, D, dev, scale_mode=SCALE_MODE)
         st = torch.randn((NUM_SLOTS, HV, D, D), generator=gen, device=dev) * 0.02
         p.load_fp32(st)
         del st
@@ -265,37 +268,56 @@ def run_ours(args, dist, rank, world, local) -> dict | None:
     if ops.device_status(clear=True):
         raise RuntimeError("device status set during the timed region")
 
-    # e2e: through the public API with pinned host buffers
+    # e2e: through the public API with pinned host buffers.  Every step copies
+    # its own inputs host -> device and its outputs device -> host; a copy
+    # stream moves step i+1's inputs while step i computes (double buffers).
     host_in = []
     for i in range(N_POOLS):
         x = inputs[i]
         host_in.append({k2: t.cpu().pin_memory() for k2, t in x.items()})
     host_slot = slot.cpu().pin_memory()
-    dev_in = {k2: torch.empty_like(t) for k2, t in inputs[0].items()}
-    dev_slot = torch.empty_like(slot)
-    host_out = torch.empty((B, HV, D), dtype=torch.bfloat16).pin_memory()
+    dev_in = [{k2: torch.empty_like(t) for k2, t in inputs[0].items()} for _ in range(2)]
+    dev_slot = [torch.empty_like(slot) for _ in range(2)]
+    dev_out = [torch.empty((B, HV, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    host_out = [torch.empty((B, HV, D), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in host_in[0].values()) + host_slot.numel() * 4
-    d2h = host_out.numel() * 2
+    d2h = host_out[0].numel() * 2
     e2e_steps = max(1, min(args.steps, 200))
+    copy_stream = torch.cuda.Stream(dev)
+    loaded = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step(i):
-        for k2 in dev_in:
-            dev_in[k2].copy_(host_in[i % N_POOLS][k2], non_blocking=True)
-        dev_slot.copy_(host_slot, non_blocking=True)
-        ops.decode(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], dev_slot,
-                   pools[i % N_POOLS], out=out)
-        host_out.copy_(out, non_blocking=True)
+    def load(i):
+        b = i % 2
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(consumed[b])
+            for k2 in dev_in[b]:
+                dev_in[b][k2].copy_(host_in[i % N_POOLS][k2], non_blocking=True)
+            dev_slot[b].copy_(host_slot, non_blocking=True)
+            loaded[b].record(copy_stream)
 
-    for i in range(3):
-        e2e_step(i)
+    def e2e_run(n):
+        for b in range(2):
+            consumed[b].record(stream)
+        load(0)
+        for i in range(n):
+            b = i % 2
+            if i + 1 < n:
+                load(i + 1)
+            stream.wait_event(loaded[b])
+            x = dev_in[b]
+            ops.decode(x["q"], x["k"], x["v"], x["g"], x["beta"], dev_slot[b], pools[i % N_POOLS], out=dev_out[b])
+            consumed[b].record(stream)
+            host_out[b].copy_(dev_out[b], non_blocking=True)
+
+    e2e_run(3)
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     _barrier(dist)
     torch.cuda.synchronize()
     e0.record(stream)
-    for i in range(e2e_steps):
-        e2e_step(i)
+    e2e_run(e2e_steps)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = _max_over_ranks(dist, e0.elapsed_time(e1))
@@ -329,6 +351,239 @@ def run_ours(args, dist, rank, world, local) -> dict | None:
     return line
 
 
+# ---- other configurations (--workload): prefill, mixed continuous batching, layer stack ----------
+
+PREFILL_SEQS, PREFILL_LEN = 8, 8192
+PREFILL_FLOP_PER_TOKEN = 5.86e6      # 32 heads x ~11.7 MFLOP per 64-token chunk / 64 (chunk-64 WY/UT form)
+PREFILL_BYTES_PER_TOKEN = 24_832     # q, k, v, o bf16 + g, beta fp32 for 32 value heads
+MIXED_PREFILLS, MIXED_DECODES, MIXED_SLOTS = 48, 512, 2048
+LAYERS, LAYER_BATCH = 36, 1024
+
+
+def _peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    return json.loads(p.read_text()) if p.exists() else {}
+
+
+def _timed(args, dist, stream, step, local):
+    """W warm-up steps, then K steps between barriers; returns (max-over-ranks
+    total ms, per-step event pairs, clock summary)."""
+    import torch
+    from gdn_b200 import ops
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if ops.device_status(clear=True):
+        raise RuntimeError("device status set during warm-up")
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    _barrier(dist)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        t0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    _barrier(dist)
+    if ops.device_status(clear=True):
+        raise RuntimeError("device status set during the timed region")
+    return _max_over_ranks(dist, t0.elapsed_time(t1)), clocks.summary()
+
+
+def _kernel_ms(args, stream, launch, reps: int = 5) -> float:
+    """Mean duration of one launch (CUDA events on its stream, after the timed run)."""
+    import torch
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(reps):
+        launch(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def _base_line(args, world, metric, value, total_ms, cfg, scaling="weak"):
+    return {"metric": metric, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "fp32 math, nvfp4 state, bf16 io",
+            "data": "synthetic", "config": cfg}
+
+
+def run_prefill(args, dist, rank, world, local) -> dict | None:
+    """Config 2: 8 sequences x 8192 tokens, zero initial state, final states to the pool."""
+    import torch
+    from gdn_b200 import NVFP4StatePool, ops, workloads
+    dev = torch.device("cuda", local)
+    T = PREFILL_SEQS * PREFILL_LEN
+    x = workloads.token_inputs(T, HK, HV, D, seed=500 + rank, device=dev)
+    cu = torch.arange(0, T + 1, PREFILL_LEN, dtype=torch.int32, device=dev)
+    pool = NVFP4StatePool.zeros(PREFILL_SEQS, HV, D, dev, scale_mode=SCALE_MODE)
+    slot = torch.arange(PREFILL_SEQS, dtype=torch.int32, device=dev)
+    out = torch.empty((T, HV, D), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        ops.prefill(x["q"], x["k"], x["v"], x["g"], x["beta"], cu, pool=pool, slot_idx=slot, out=out)
+
+    total_ms, clocks = _timed(args, dist, stream, step, local)
+    launch_ms = _max_over_ranks(dist, _kernel_ms(args, stream, step))
+    # e2e: host inputs in, outputs back, every step (sequential: the inputs are 1.6 GB)
+    host = {k2: t.cpu().pin_memory() for k2, t in x.items()}
+    host_out = torch.empty((T, HV, D), dtype=torch.bfloat16).pin_memory()
+    dev_in = {k2: torch.empty_like(t) for k2, t in x.items()}
+    e2e_steps = 3
+
+    def e2e_step(i):
+        for k2 in dev_in:
+            dev_in[k2].copy_(host[k2], non_blocking=True)
+        ops.prefill(dev_in["q"], dev_in["k"], dev_in["v"], dev_in["g"], dev_in["beta"], cu, pool=pool,
+                    slot_idx=slot, out=out)
+        host_out.copy_(out, non_blocking=True)
+
+    e2e_step(0)
+    torch.cuda.synchronize()
+    e_ms = _max_over_ranks(dist, _kernel_ms(args, stream, e2e_step, e2e_steps))
+    if rank != 0:
+        return None
+    tokens = T * world
+    peaks = _peaks()
+    flops = PREFILL_FLOP_PER_TOKEN * T
+    tf = flops / (launch_ms / 1e3) / 1e12
+    tpeak = peaks.get("bf16_tflops", 1590.0)
+    gbs = PREFILL_BYTES_PER_TOKEN * T / (launch_ms / 1e3) / 1e9
+    hpeak = peaks.get("hbm_gbs", 6650.0)
+    cfg = {"workload": "prefill_8x8192_chunk64_hk16_hv32_d128", "sequences_per_gpu": PREFILL_SEQS,
+           "seq_len": PREFILL_LEN, "chunk": 64, "initial_state": "zero", "final_state": "nvfp4 pool",
+           "parallelism": f"dp{world} (sequences sharded, no collective)", "l2": "inputs 1.6 GB > L2"}
+    line = _base_line(args, world, "GDN prefill tokens/s (chunk 64, 8 x 8192 tokens)", tokens / (total_ms / args.steps
+                      / 1e3), total_ms, cfg)
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    line.update({
+        "e2e": {"value": round(tokens / (e_ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": host_out.numel() * 2},
+        "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": tpeak, "unit": "TFLOP/s",
+                     "frac": round(tf / tpeak, 4), "traffic": None, "kernel": "gdn_prefill_kernel",
+                     "mean_launch_us": round(launch_ms * 1e3, 2),
+                     "hbm": {"achieved": round(gbs, 1), "peak": hpeak, "frac": round(gbs / hpeak, 4)}},
+        "gpu_launches": args.steps, "clocks": clocks})
+    return line
+
+
+def run_mixed(args, dist, rank, world, local) -> dict | None:
+    """Config 3: 48 varlen prefills (U[128, 4096]) + 512 decodes per step on a
+    2048-slot pool addressed through a seeded random permutation.  The prefill
+    and decode kernels run on two streams."""
+    import torch
+    from gdn_b200 import NVFP4StatePool, ops, workloads
+    dev = torch.device("cuda", local)
+    lengths = workloads.varlen_lengths(MIXED_PREFILLS, 128, 4096, seed=7 + rank)
+    Tp = sum(lengths)
+    xp = workloads.token_inputs(Tp, HK, HV, D, seed=600 + rank, device=dev)
+    cu = torch.tensor([0] + list(__import__("itertools").accumulate(lengths)), dtype=torch.int32, device=dev)
+    xd = {k2: t[0] for k2, t in workloads.decode_steps(MIXED_DECODES, 1, HK, HV, D, seed=700 + rank,
+                                                        device=dev).items()}
+    perm = workloads.slot_permutation(MIXED_PREFILLS + MIXED_DECODES, MIXED_SLOTS, seed=8 + rank).to(dev)
+    slot_p, slot_d = perm[:MIXED_PREFILLS].contiguous(), perm[MIXED_PREFILLS:].contiguous()
+    pool = NVFP4StatePool.zeros(MIXED_SLOTS, HV, D, dev, scale_mode=SCALE_MODE)
+    gen = torch.Generator(device=dev).manual_seed(900 + rank)
+    for c in range(0, MIXED_SLOTS, 256):
+        pool.load_fp32(torch.randn((256, HV, D, D), generator=gen, device=dev) * 0.02,
+                       torch.arange(c, c + 256, dtype=torch.int32, device=dev))
+    out_p = torch.empty((Tp, HV, D), dtype=torch.bfloat16, device=dev)
+    out_d = torch.empty((MIXED_DECODES, HV, D), dtype=torch.bfloat16, device=dev)
+    main = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    fork = torch.cuda.Event()
+    join = torch.cuda.Event()
+
+    def step(i):
+        fork.record(main)
+        side.wait_event(fork)
+        ops.prefill(xp["q"], xp["k"], xp["v"], xp["g"], xp["beta"], cu, pool=pool, slot_idx=slot_p, out=out_p)
+        with torch.cuda.stream(side):
+            ops.decode(xd["q"], xd["k"], xd["v"], xd["g"], xd["beta"], slot_d, pool, out=out_d)
+            join.record(side)
+        main.wait_event(join)
+
+    total_ms, clocks = _timed(args, dist, main, step, local)
+    pre_ms = _kernel_ms(args, main, lambda i: ops.prefill(xp["q"], xp["k"], xp["v"], xp["g"], xp["beta"], cu,
+                                                          pool=pool, slot_idx=slot_p, out=out_p))
+    dec_ms = _kernel_ms(args, main, lambda i: ops.decode(xd["q"], xd["k"], xd["v"], xd["g"], xd["beta"], slot_d,
+                                                         pool, out=out_d))
+    if rank != 0:
+        return None
+    tokens = (Tp + MIXED_DECODES) * world
+    peaks = _peaks()
+    cfg = {"workload": "mixed_48prefill_u128_4096_512decode_pool2048_perm", "prefill_tokens": Tp,
+           "decode_sequences": MIXED_DECODES, "pool_slots": MIXED_SLOTS, "streams": "prefill || decode",
+           "parallelism": f"dp{world} (sequences sharded, no collective)"}
+    line = _base_line(args, world, "GDN mixed continuous-batching tokens/s (prefill + decode)",
+                      tokens / (total_ms / args.steps / 1e3), total_ms, cfg)
+    dec_gbs = BYTES_PER_TOKEN * MIXED_DECODES / (dec_ms / 1e3) / 1e9
+    pre_tf = PREFILL_FLOP_PER_TOKEN * Tp / (pre_ms / 1e3) / 1e12
+    line.update({
+        "roofline": {"bound": "tensor", "achieved": round(pre_tf, 1), "peak": peaks.get("bf16_tflops", 1590.0),
+                     "unit": "TFLOP/s", "frac": round(pre_tf / peaks.get("bf16_tflops", 1590.0), 4), "traffic": None,
+                     "kernel": "gdn_prefill_kernel", "mean_launch_us": round(pre_ms * 1e3, 2),
+                     "decode": {"achieved_gbs": round(dec_gbs, 1), "frac": round(dec_gbs / peaks.get("hbm_gbs",
+                                6650.0), 4), "mean_launch_us": round(dec_ms * 1e3, 2)}},
+        "gpu_launches": 2 * args.steps, "clocks": clocks})
+    return line
+
+
+def run_layers(args, dist, rank, world, local) -> dict | None:
+    """Config 4: 36 GDN layers, batch 1024 decode, value heads sharded over the
+    ranks (TP = world: 32/world value and 16/world key heads per GPU), one
+    NVFP4 pool of 1024 slots per layer with a seeded random slot map.  Total
+    work is fixed as the rank count grows (strong scaling)."""
+    import torch
+    from gdn_b200 import NVFP4StatePool, ops, workloads
+    dev = torch.device("cuda", local)
+    if HV % world or HK % world:
+        raise ValueError("the rank count must divide the head counts")
+    hv, hk = HV // world, HK // world
+    pools, slots, inputs = [], [], []
+    gen = torch.Generator(device=dev)
+    for layer in range(LAYERS):
+        gen.manual_seed(10_000 * rank + layer)
+        p = NVFP4StatePool.zeros(LAYER_BATCH, hv, D, dev, scale_mode=SCALE_MODE)
+        for c in range(0, LAYER_BATCH, 256):
+            p.load_fp32(torch.randn((256, hv, D, D), generator=gen, device=dev) * 0.02,
+                        torch.arange(c, c + 256, dtype=torch.int32, device=dev))
+        pools.append(p)
+        slots.append(workloads.slot_permutation(LAYER_BATCH, LAYER_BATCH, seed=20_000 + layer).to(dev))
+        inputs.append({k2: t[0] for k2, t in workloads.decode_steps(LAYER_BATCH, 1, hk, hv, D,
+                                                                     seed=30_000 + 100 * layer + rank,
+                                                                     device=dev).items()})
+    out = torch.empty((LAYER_BATCH, hv, D), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        for layer in range(LAYERS):
+            x = inputs[layer]
+            ops.decode(x["q"], x["k"], x["v"], x["g"], x["beta"], slots[layer], pools[layer], out=out)
+
+    total_ms, clocks = _timed(args, dist, stream, step, local)
+    launch_ms = _max_over_ranks(dist, _kernel_ms(args, stream, step) / LAYERS)
+    if rank != 0:
+        return None
+    peaks = _peaks()
+    gbs = BYTES_PER_TOKEN * (hv / HV) * LAYER_BATCH / (launch_ms / 1e3) / 1e9
+    cfg = {"workload": "layers36_decode_b1024_hk16_hv32_d128_tp", "layers": LAYERS, "batch": LAYER_BATCH,
+           "v_heads_per_gpu": hv, "k_heads_per_gpu": hk, "parallelism": f"tp{world} (value heads sharded)",
+           "pool": "per-layer 1024 slots, random slot map"}
+    line = _base_line(args, world, "GDN 36-layer decode tokens/s (batch 1024)",
+                      LAYER_BATCH / (total_ms / args.steps / 1e3), total_ms, cfg, scaling="strong")
+    line.update({
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks.get("hbm_gbs", 6650.0),
+                     "unit": "GB/s", "frac": round(gbs / peaks.get("hbm_gbs", 6650.0), 4), "traffic": None,
+                     "kernel": "gdn_decode_kernel", "mean_launch_us": round(launch_ms * 1e3, 2)},
+        "gpu_launches": LAYERS * args.steps, "clocks": clocks})
+    return line
+
+
 def run_reference(args, rank) -> dict | None:
     if rank != 0:
         return None
@@ -359,6 +614,9 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", choices=["decode", "prefill", "mixed", "layers"], default="decode",
+                    help="decode: batch-256 decode step (the headline); prefill: 8 x 8192-token chunked "
+                         "prefill; mixed: 48 varlen prefills + 512 decodes; layers: 36-layer TP decode stack")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -369,7 +627,8 @@ def main() -> None:
         return
     dist, rank, world, local = _dist_init(args.gpus)
     try:
-        line = run_ours(args, dist, rank, world, local)
+        runner = {"decode": run_ours, "prefill": run_prefill, "mixed": run_mixed, "layers": run_layers}
+        line = runner[args.workload](args, dist, rank, world, local)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:

@@ -169,6 +169,78 @@ at::Tensor decode_meta(const at::Tensor& q, const at::Tensor&, const at::Tensor&
   return at::empty({q.size(0), v.size(1), q.size(2)}, q.options());
 }
 
+// ---- chunked prefill over packed variable-length sequences --------------------------------
+
+at::Tensor prefill_cuda(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
+                        const at::Tensor& beta, const at::Tensor& cu_seqlens,
+                        const c10::optional<at::Tensor>& slot_idx, const c10::optional<at::Tensor>& has_initial_state,
+                        at::Tensor& pool_codes, at::Tensor& pool_scales, at::Tensor& pool_gscale, double q_scale,
+                        int64_t scale_mode, double gscale_den) {
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.dim() == 3, "q, k, v must be [T, heads, D]");
+  const int64_t T = q.size(0), HK = q.size(1), D = q.size(2), HV = v.size(1);
+  for (const at::Tensor* t : {&q, &k, &v}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16, "q, k, v must be CUDA bfloat16");
+    TORCH_CHECK(t->stride(2) == 1 && t->stride(1) == D, "q, k, v heads must be contiguous");
+  }
+  TORCH_CHECK(k.sizes() == q.sizes() && v.size(0) == T && v.size(2) == D, "q, k, v shape mismatch");
+  need(g, at::kFloat, "g");
+  need(beta, at::kFloat, "beta");
+  need(cu_seqlens, at::kInt, "cu_seqlens");
+  TORCH_CHECK(g.numel() == T * HV && beta.numel() == T * HV, "g/beta must be [T, HV]");
+  const int64_t N = cu_seqlens.numel() - 1;
+  TORCH_CHECK(N >= 0, "cu_seqlens needs N + 1 entries");
+  c10::cuda::CUDAGuard guard(q.device());
+  at::Tensor out = at::empty({T, HV, D}, q.options());
+  gdn_prefill_params p{};
+  p.num_seqs = (int32_t)N;
+  p.num_k_heads = (int32_t)HK;
+  p.num_v_heads = (int32_t)HV;
+  p.head_dim = (int32_t)D;
+  p.total_tokens = T;
+  p.q = reinterpret_cast<const gdn_bf16_t*>(q.data_ptr());
+  p.k = reinterpret_cast<const gdn_bf16_t*>(k.data_ptr());
+  p.v = reinterpret_cast<const gdn_bf16_t*>(v.data_ptr());
+  p.q_stride = q.stride(0);
+  p.k_stride = k.stride(0);
+  p.v_stride = v.stride(0);
+  p.g = g.data_ptr<float>();
+  p.beta = beta.data_ptr<float>();
+  p.cu_seqlens = cu_seqlens.data_ptr<int32_t>();
+  if (has_initial_state.has_value()) {
+    need(*has_initial_state, at::kBool, "has_initial_state");
+    TORCH_CHECK(has_initial_state->numel() == N, "has_initial_state must be [N]");
+    p.has_initial_state = reinterpret_cast<const uint8_t*>(has_initial_state->data_ptr());
+  }
+  if (slot_idx.has_value()) {
+    need(*slot_idx, at::kInt, "slot_idx");
+    TORCH_CHECK(slot_idx->numel() == N, "slot_idx must be [N]");
+    need(pool_codes, at::kByte, "pool_codes");
+    need(pool_scales, at::kByte, "pool_scales");
+    need(pool_gscale, at::kFloat, "pool_gscale");
+    TORCH_CHECK(pool_codes.dim() == 4 && pool_codes.size(1) == HV && pool_codes.size(2) == D &&
+                    pool_codes.size(3) == D / 2,
+                "pool_codes must be [slots, HV, D, D/2]");
+    p.num_slots = pool_codes.size(0);
+    p.slot_idx = slot_idx->data_ptr<int32_t>();
+    p.pool_codes = pool_codes.data_ptr<uint8_t>();
+    p.pool_scales = pool_scales.data_ptr<uint8_t>();
+    p.pool_gscale = pool_gscale.data_ptr<float>();
+  }
+  p.out = reinterpret_cast<gdn_bf16_t*>(out.data_ptr());
+  p.q_scale = (float)q_scale;
+  p.scale_mode = (int32_t)scale_mode;
+  p.gscale_den = (float)gscale_den;
+  check_rc(gdn_prefill(&p, cur_stream(q)), "gdn_prefill");
+  return out;
+}
+
+at::Tensor prefill_meta(const at::Tensor& q, const at::Tensor&, const at::Tensor& v, const at::Tensor&,
+                        const at::Tensor&, const at::Tensor&, const c10::optional<at::Tensor>&,
+                        const c10::optional<at::Tensor>&, at::Tensor&, at::Tensor&, at::Tensor&, double, int64_t,
+                        double) {
+  return at::empty({q.size(0), v.size(1), q.size(2)}, q.options());
+}
+
 }  // namespace
 
 TORCH_LIBRARY(gdn_sm120, m) {
@@ -179,6 +251,9 @@ TORCH_LIBRARY(gdn_sm120, m) {
   m.def("decode(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor slot_idx, "
         "Tensor(a!) pool_codes, Tensor(b!) pool_scales, Tensor(c!) pool_gscale, "
         "float q_scale=0., int scale_mode=0, float gscale_den=0.) -> Tensor");
+  m.def("prefill(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor cu_seqlens, Tensor? slot_idx, "
+        "Tensor? has_initial_state, Tensor(a!) pool_codes, Tensor(b!) pool_scales, Tensor(c!) pool_gscale, "
+        "float q_scale=0., int scale_mode=0, float gscale_den=0.) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(gdn_sm120, CUDA, m) {
@@ -186,6 +261,7 @@ TORCH_LIBRARY_IMPL(gdn_sm120, CUDA, m) {
   m.impl("nvfp4_quantize", &quantize_cuda);
   m.impl("nvfp4_dequantize", &dequantize_cuda);
   m.impl("decode", &decode_cuda);
+  m.impl("prefill", &prefill_cuda);
 }
 
 TORCH_LIBRARY_IMPL(gdn_sm120, Meta, m) {
@@ -193,4 +269,5 @@ TORCH_LIBRARY_IMPL(gdn_sm120, Meta, m) {
   m.impl("nvfp4_quantize", &quantize_meta);
   m.impl("nvfp4_dequantize", &dequantize_meta);
   m.impl("decode", &decode_meta);
+  m.impl("prefill", &prefill_meta);
 }

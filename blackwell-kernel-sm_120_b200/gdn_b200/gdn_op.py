@@ -98,3 +98,18 @@ def decode(q, k, v, g, beta, slot_idx, pool, q_scale: float = 0.0) -> torch.Tens
     load_gdn_op()
     return torch.ops.gdn_sm120.decode(q, k, v, g, beta, slot_idx, pool.codes, pool.scales, pool.gscale,
                                       q_scale, pool.scale_mode, pool.gscale_den)
+
+
+def prefill(q, k, v, g, beta, cu_seqlens, pool=None, slot_idx=None, has_initial_state=None,
+            q_scale: float = 0.0) -> torch.Tensor:
+    """Chunked gated-delta-rule prefill through torch.ops.gdn_sm120.prefill.
+    With a pool and slot_idx, sequence n starts from slot_idx[n] when
+    has_initial_state[n] and leaves its final state there."""
+    load_gdn_op()
+    if pool is None:
+        empty_u8 = torch.empty(0, dtype=torch.uint8, device=q.device)
+        empty_f = torch.empty(0, dtype=torch.float32, device=q.device)
+        return torch.ops.gdn_sm120.prefill(q, k, v, g, beta, cu_seqlens, None, has_initial_state, empty_u8,
+                                           empty_u8, empty_f, q_scale, 0, 0.0)
+    return torch.ops.gdn_sm120.prefill(q, k, v, g, beta, cu_seqlens, slot_idx, has_initial_state, pool.codes,
+                                       pool.scales, pool.gscale, q_scale, pool.scale_mode, pool.gscale_den)

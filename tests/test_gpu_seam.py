@@ -1,0 +1,105 @@
+"""GPU checks of the vLLM 0.22 seam (gdn_b200.vllm_seam) and of the
+gdn_sm120.prefill torch op: same kernels as the C ABI, vLLM's argument
+conventions ([1, T, H, D] inputs, [N, HV, V, K] dense states, PAD_SLOT_ID=-1)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+HK, HV, D = 16, 32, 128
+QS = 1.0 / np.sqrt(D)
+
+
+def _inputs(lengths, seed):
+    from gdn_b200 import workloads
+    x = workloads.token_inputs(int(sum(lengths)), HK, HV, D, seed=seed, device="cuda")
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int32, device="cuda")
+    return x, cu
+
+
+def test_torch_prefill_op_matches_capi(cuda):
+    from gdn_b200 import gdn_op, ops, NVFP4StatePool, workloads
+    x, cu = _inputs([70, 5, 130], seed=21)
+    o1 = ops.prefill(x["q"], x["k"], x["v"], x["g"], x["beta"], cu)
+    o2 = gdn_op.prefill(x["q"], x["k"], x["v"], x["g"], x["beta"], cu)
+    assert torch.equal(o1, o2)
+    states = workloads.initial_states(4, HV, D, seed=3).cuda()
+    p1 = NVFP4StatePool.zeros(4, HV, D, "cuda")
+    p1.load_fp32(states)
+    p2 = NVFP4StatePool.zeros(4, HV, D, "cuda")
+    p2.load_fp32(states)
+    slot = torch.tensor([2, 0, 3], dtype=torch.int32, device="cuda")
+    has = torch.tensor([True, False, True], device="cuda")
+    o1 = ops.prefill(x["q"], x["k"], x["v"], x["g"], x["beta"], cu, pool=p1, slot_idx=slot, has_initial_state=has)
+    o2 = gdn_op.prefill(x["q"], x["k"], x["v"], x["g"], x["beta"], cu, pool=p2, slot_idx=slot, has_initial_state=has)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2)
+    assert torch.equal(p1.codes, p2.codes) and torch.equal(p1.gscale, p2.gscale)
+
+
+def test_seam_prefill(cuda):
+    from gdn_b200 import ops, vllm_seam, workloads
+    from oracle import bindings as ob
+    lengths = [100, 33]
+    x, cu = _inputs(lengths, seed=22)
+    N = len(lengths)
+    init = workloads.initial_states(N, HV, D, seed=4).cuda()      # S[k][v]
+    init_vk = init.transpose(-1, -2).contiguous()                   # vLLM layout [V][K]
+    o, final = vllm_seam.chunk_gated_delta_rule(
+        x["q"].unsqueeze(0), x["k"].unsqueeze(0), x["v"].unsqueeze(0), x["g"].unsqueeze(0),
+        x["beta"].unsqueeze(0), init_vk, True, cu_seqlens=cu, use_qk_l2norm_in_kernel=False)
+    torch.cuda.synchronize()
+    assert o.shape == (1, sum(lengths), HV, D) and final.shape == (N, HV, D, D)
+    # reference: f64 recurrence from the NVFP4-rounded initial states
+    from gdn_b200 import NVFP4StatePool
+    pool = NVFP4StatePool.zeros(N, HV, D, "cuda")
+    pool.load_fp32(init)
+    S0 = pool.dequantize().cpu().numpy()
+    q, k, v = (x[n].float().cpu().numpy() for n in ("q", "k", "v"))
+    g, be = x["g"].cpu().numpy(), x["beta"].cpu().numpy()
+    cun = cu.cpu().numpy()
+    on = o[0].float().cpu().numpy()
+    fin = final.transpose(-1, -2).cpu().numpy()
+    for n in range(N):
+        b0, b1 = cun[n], cun[n + 1]
+        for h in range(0, HV, 7):
+            ref, S = ob.recurrent_f64(S0[n, h], q[b0:b1, h // 2], k[b0:b1, h // 2], v[b0:b1, h], g[b0:b1, h],
+                                      be[b0:b1, h], QS)
+            assert np.linalg.norm(on[b0:b1, h] - ref) <= 1e-2 * np.linalg.norm(ref)
+            # final state crosses NVFP4 once more on the way out
+            assert np.linalg.norm(fin[n, h] - S) <= 0.15 * np.linalg.norm(S)
+
+
+def test_seam_decode_in_place(cuda):
+    from gdn_b200 import ops, vllm_seam, NVFP4StatePool, workloads
+    B, slots = 6, 10
+    x = workloads.decode_steps(B, 1, HK, HV, D, seed=23, device="cuda")
+    gen = torch.Generator(device="cpu").manual_seed(5)
+    A_log = torch.randn(HV, generator=gen).cuda()
+    dt_bias = torch.randn(HV, generator=gen).cuda()
+    a = torch.randn(B, HV, generator=gen).cuda()
+    b = torch.randn(B, HV, generator=gen).cuda()
+    ssm = workloads.initial_states(slots, HV, D, seed=6).cuda().transpose(-1, -2).contiguous()  # [slots, HV, V, K]
+    before = ssm.clone()
+    idx = torch.tensor([4, -1, 0, 9, 2, 7], dtype=torch.int32, device="cuda")
+    o, st = vllm_seam.fused_sigmoid_gating_delta_rule_update(
+        A_log, a, b, dt_bias, x["q"][0].unsqueeze(0), x["k"][0].unsqueeze(0), x["v"][0].unsqueeze(0), ssm,
+        inplace_final_state=True, ssm_state_indices=idx, use_qk_l2norm_in_kernel=False)
+    torch.cuda.synchronize()
+    assert st is ssm and o.shape == (1, B, HV, D)
+    # same kernel through the C ABI on the same NVFP4 tiles
+    g, beta = vllm_seam.gating(A_log, a, b, dt_bias)
+    pool = NVFP4StatePool.zeros(B, HV, D, "cuda")
+    pool.load_fp32(before[idx.long().clamp(min=0)].transpose(-1, -2).contiguous())
+    slot = torch.tensor([0, -1, 2, 3, 4, 5], dtype=torch.int32, device="cuda")
+    o_ref = ops.decode(x["q"][0], x["k"][0], x["v"][0], g, beta, slot, pool)
+    assert torch.equal(o[0], o_ref)
+    new = pool.dequantize().transpose(-1, -2)
+    for i, s in enumerate(idx.tolist()):
+        if s >= 0:
+            assert torch.equal(ssm[s], new[i])
+    for s in (1, 3, 5, 6, 8):
+        assert torch.equal(ssm[s], before[s])
