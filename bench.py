@@ -152,10 +152,8 @@ def _barrier(dist):
 def _max_over_ranks(dist, x: float) -> float:
     if dist is None:
         return x
-    import torch
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from gdn_b200 import sharding
+    return sharding.max_over_ranks(x)
 
 
 # ---- CPU path ---------------------------------------------------------------------------------
@@ -541,9 +539,9 @@ def run_layers(args, dist, rank, world, local) -> dict | None:
     import torch
     from gdn_b200 import NVFP4StatePool, ops, workloads
     dev = torch.device("cuda", local)
-    if HV % world or HK % world:
-        raise ValueError("the rank count must divide the head counts")
-    hv, hk = HV // world, HK // world
+    from gdn_b200 import sharding
+    hv_shard, hk_shard = sharding.shard_heads(HV, HK, rank, world)
+    hv, hk = hv_shard.size, hk_shard.size
     pools, slots, inputs = [], [], []
     gen = torch.Generator(device=dev)
     for layer in range(LAYERS):
