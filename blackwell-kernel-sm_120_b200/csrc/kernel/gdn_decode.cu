@@ -1,42 +1,42 @@
 // gdn_decode.cu -- fused recurrent NVFP4 Gated DeltaNet decode step (sm_100a).
 //
-// One CTA owns one (sequence, value head) state tile at a time: a 128 x 128
-// NVFP4 tile S[i][j] (i over d_k, j over d_v; 8192 B codes + 1024 B scales +
-// one fp32 global scale) in the pool slot named by slot_idx.  Per tile:
+// Per (sequence, value head) tile -- a 128 x 128 NVFP4 state S[i][j] (i over
+// d_k, j over d_v; 8192 B codes + 1024 B scales + one fp32 global scale gs)
+// in the pool slot named by slot_idx:
 //   alpha = exp(g), S_a = alpha S, u = S_a^T k, w = beta (v - u),
 //   S' = S_a + k w^T, o = q_scale S'^T q = q_scale (S_a^T q + (k.q) w),
 // then S' is requantised in place with a fresh global scale
 // gs' = amax(S') / gden and the reference block quantiser
-// (src/kernel/gdn_state_update_ref.cu:93-141) applied to y = S' (1/gs').
+// (src/kernel/gdn_state_update_ref.cu:93-141) applied to y = S' / gs'.
 // The reference has no counterpart of this step (its only update is
 // S' = alpha S + beta k v^T, gdn_state_update_ref.cu:51-67); the recurrence is
 // the gated delta rule (Yang, Kautz & Hatamizadeh, ICLR 2025).
 //
-// The tensor cores decode the tile twice, both times exactly, with one
-// block-scaled E2M1 MMA (kind::mxf4nvf4) against a constant identity operand:
-//   MMA1' D = I * S^T with the tile's E4M3 scales as B scale factors
-//         -> e2m1 * scale with TMEM lane = j, column = i.  Each thread then
-//         holds one column j over 64 rows i and forms its partial sums of
-//         u = S_a^T k and S_a^T q with packed f32x2 FMAs (no reduction across
-//         lanes; the two row halves meet in shared memory);
-//   MMA1  D = S * I with the scales as A scale factors -> lane = i, column = j,
-//         the layout the requantiser wants: each thread holds one row i and
-//         64 columns j, i.e. four whole 16-element scale blocks.
-// The identity operand and its unit scale factors are built once per CTA.
-// MMA1 runs while the threads compute the partial sums; the next tile's
-// operands are staged and its MMA1' issued before the current tile is
-// updated and requantised, so the tensor-core round trips overlap SIMT work.
-// Requantisation uses cvt.rn.satfinite.e2m1x2.f32 with the tie correction of
-// intrinsics/nvfp4_codec.cuh; all element arithmetic is packed f32x2.
+// The decode and the rank-1 update run on the tensor cores.  With
+// c = alpha gs and S_dq = e2m1 * block scale (so S = gs S_dq):
+//   MMA1'   D1' = I * S_dq^T          block-scaled E2M1 MMA against an identity
+//                                     (lane = column j; double-buffered)
+//   SIMT    [u p] / c = D1' [k q]     each w thread reduces its own row of D1'
+//   MMA1    D1  = S_dq * I            the tile again, lane = row i
+//   MMA_r1  D1 += k (w / c)^T         tf32 rank-1 update, w / c split hi + lo
+// so S' = c D1 and the requantiser reads y = D1 * (c / gs') straight from TMEM.
+// The codes arrive by one 2-D TMA copy with 64-byte swizzle that both decode
+// MMAs read in place.
 //
-// Pipeline: persistent grid of 2 CTAs per SM (256 TMEM columns each); a
-// 4-stage ring of 1-D bulk copies prefetches the next tiles' codes, scales,
-// q, k, v; per-tile scalars are loaded one tile ahead; every wait is bounded.
-//
-// Scale bytes are read by the tensor cores as UE4M3: identical to the
-// reference decode for every byte the quantiser writes (0x00..0x77 in the
-// reference mode, 0x00..0x7E in the E4M3FN mode).
+// Warp roles (one CTA per SM, 14 warps):
+//   warp 13     producer: walks the CTA's tiles, loads the per-tile scalars,
+//               queues the TMA copies into a 6-stage ring, zeroes the outputs
+//               of padding tiles;
+//   warp 12     MMA: scale-factor permutation, the [k q] operand, every MMA
+//               and commit; it issues tile n+1's MMA1' before waiting for
+//               tile n's w;
+//   warps 8-11  w: u, p -> w, o (stored) and the rank-1 operand;
+//   warps 0-7   requantise D1 and store the tile.
+// Every wait is bounded; a timeout in any role stops all of them.
 #include <cstdint>
+#include <mutex>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 
 #include "../common.cuh"
@@ -48,46 +48,77 @@ namespace gdn {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-constexpr int kStages = 4;
+constexpr int kQWarps = 8;
+constexpr int kWWarp0 = 8;
+constexpr int kMmaWarp = 12;
+constexpr int kProdWarp = 13;
+constexpr int kThreads = 14 * 32;
+constexpr int kStages = 6;
 constexpr uint32_t kCodeBytes = kD * kD / 2;    // 8192
 constexpr uint32_t kScaleBytes = kD * kD / 16;  // 1024
 constexpr uint32_t kVecBytes = kD * 2;          // 256
 constexpr uint32_t kStageTx = kCodeBytes + kScaleBytes + 3 * kVecBytes;
-constexpr uint32_t kTmemCols = 256;
-// TMEM columns
-constexpr uint32_t kColD = 0;      // 128: dequantised tile (transposed, then not)
-constexpr uint32_t kColSF = 128;   // 8: the tile's scale factors (2 K-steps x 4 columns)
-constexpr uint32_t kColOne = 136;  // 8: unit scale factors of the identity
+constexpr float kDropBelow = 1e-30f;            // alpha * gs below this: the decayed state is zero
 
-struct __align__(128) Stage {
-  uint8_t codes[kCodeBytes];  // row-major, 64 B per row
+// TMEM columns (512 allocated)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColD1 = 0;     // 128: D1 (lane i)
+constexpr uint32_t kColD1t = 128;  // 2 x 128: D1' (lane j), double-buffered
+constexpr uint32_t kColSF = 384;   // 3 x 8: the tile's scale factors (tile n uses n % 3: the
+                                   // slot is rewritten only after tile n - 3's MMA1 is known complete)
+constexpr uint32_t kColOne = 408;  // 8: unit scale factors of the identity
+
+struct TileMeta {
+  int64_t pt;       // slot * HV + h
+  int32_t b, h;
+  float c;          // alpha * gs (1 when the decayed state is dropped)
+  float inv_c;
+  float beta;
+  int32_t drop;     // alpha * gs < kDropBelow: S_a = 0
+  int32_t end;      // no more tiles
+};
+
+struct __align__(1024) Stage {
+  uint8_t codes[kCodeBytes];  // 64-byte swizzled rows (TMA), read in place by MMA1' and MMA1
   uint8_t scales[kScaleBytes];
   __nv_bfloat16 q[kD];
   __nv_bfloat16 k[kD];
   __nv_bfloat16 v[kD];
+  TileMeta meta;
+};
+
+struct InfoW {
+  TileMeta m;
+  float kq;
+  int32_t stage;
 };
 
 struct __align__(1024) DecodeSmem {
   Stage st[kStages];
-  // MMA operands, no-swizzle K-major layout: byte b of row r at
-  // (b % 16) + 16 r + 2048 (b / 16).
-  uint8_t codes[kCodeBytes];
-  uint8_t ident[kCodeBytes];
-  uint8_t sf[kScaleBytes];  // scale factors, tcgen05.cp 32x128b layout, 2 K-steps
+  uint8_t ident[kCodeBytes];  // identity, no-swizzle K-major: byte b of row r at (b % 16) + 16 r + 2048 (b / 16)
   uint8_t sf_one[kScaleBytes];
-  float4 kq4[kD / 2];       // (k_i, k_i+1, q_i, q_i+1) for even i: the matvec operands
-  float red[2][2][kD];      // [row half][u or S^T q][column]
-  float w[kD];
-  float amax[kWarps];
+  uint8_t sfb[2][kScaleBytes];  // tcgen05.cp 32x128b layout, 2 K-steps
+  float4 kq4[2][kD / 2];        // (k_i, k_i+1, q_i, q_i+1), even i
+  uint8_t ak[2][kD * 8 * 4];    // [128][8] fp32 K-major: columns 0, 1 = k
+  uint8_t bw[2][kD * 8 * 4];    // [128][8] fp32 K-major: columns 0, 1 = hi, lo of w / c
+  InfoW iw[2];
+  TileMeta iq;
+  float amax[2][kQWarps];
   float inv_tab[256];
-  uint64_t full[kStages];
-  uint64_t bar_dt, bar_d;
+  uint64_t full[kStages], empty[kStages], bar_t[2], bar_w, bar_d, bar_q, bar_fin;
   uint32_t tmem_base;
+  int abort_flag;
 };
 
 __device__ __forceinline__ int canon(int row, int byte) { return (byte & 15) + 16 * row + 2048 * (byte >> 4); }
+// [rows][K] fp32 K-major, 16-byte K chunks 128 bytes apart, 8-row groups sbo apart.
+__device__ __forceinline__ uint32_t kf32(int row, int k, uint32_t sbo) {
+  return (row & 7) * 16 + (k & 3) * 4 + (row >> 3) * sbo + (k >> 2) * 128;
+}
+__device__ __forceinline__ uint64_t desc_codes(const uint8_t* codes, int kstep) {
+  // K-major, 64-byte swizzle: 8-row groups 512 bytes apart, K step = 32 bytes (64 E2M1 values)
+  return tc::smem_desc(codes + 32 * kstep, 16, 512) | (4ull << 61);
+}
 
 struct DecodeArgs {
   int32_t B, HK, HV, group;
@@ -106,40 +137,20 @@ struct DecodeArgs {
   float q_scale, gden;
   float* debug_y;
   uint32_t* status;
-  // Tile t = b * HV + h.  A CTA visits t = blockIdx.x + n * gridDim.x; the
-  // (b, h) step between visits is precomputed on the host so the kernel never
-  // divides.
-  int32_t step_b, step_h;
 };
 
-// (sequence, value head) of a tile, advanced without division.
-struct TileIdx {
-  int32_t b, h;
-  __device__ __forceinline__ void advance(int32_t db, int32_t dh, int32_t HV) {
-    h += dh;
-    b += db;
-    if (h >= HV) { h -= HV; ++b; }
+// Bounded wait that also gives up when another role has aborted.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      *abort_flag = 1;
+      return false;
+    }
   }
-};
-
-// Thread 0: queue the tile (t.b, t.h) into stage `s`.
-__device__ __forceinline__ void issue_tile(const DecodeArgs& a, DecodeSmem& sm, int s, TileIdx t) {
-  const int b = t.b, h = t.h;
-  const int32_t slot = __ldg(a.slot_idx + b);
-  uint64_t* bar = &sm.full[s];
-  if (slot < 0 || slot >= a.num_slots) {
-    mbar_arrive(bar);  // nothing to load: complete the phase
-    return;
-  }
-  const int hk = h / a.group;
-  const int64_t pt = (int64_t)slot * a.HV + h;
-  Stage& st = sm.st[s];
-  mbar_arrive_expect_tx(bar, kStageTx);
-  bulk_g2s(st.codes, a.pool_codes + pt * kCodeBytes, kCodeBytes, bar);
-  bulk_g2s(st.scales, a.pool_scales + pt * kScaleBytes, kScaleBytes, bar);
-  bulk_g2s(st.q, a.q + b * a.q_stride + (int64_t)hk * kD, kVecBytes, bar);
-  bulk_g2s(st.k, a.k + b * a.k_stride + (int64_t)hk * kD, kVecBytes, bar);
-  bulk_g2s(st.v, a.v + b * a.v_stride + (int64_t)h * kD, kVecBytes, bar);
 }
 
 __device__ __forceinline__ uint16_t f2bf_bits(float f) {
@@ -147,45 +158,20 @@ __device__ __forceinline__ uint16_t f2bf_bits(float f) {
   return *reinterpret_cast<const uint16_t*>(&b);
 }
 
-struct Scalars {
-  int32_t slot;
-  float gs, g, beta;
-};
-
-__device__ __forceinline__ Scalars load_scalars(const DecodeArgs& a, TileIdx t) {
-  Scalars sc{-1, 0.0f, 0.0f, 0.0f};
-  if (t.b < a.B) {
-    const int b = t.b, h = t.h;
-    sc.slot = __ldg(a.slot_idx + b);
-    sc.g = __ldg(a.g + (int64_t)b * a.HV + h);
-    sc.beta = __ldg(a.beta + (int64_t)b * a.HV + h);
-    if (sc.slot >= 0 && sc.slot < a.num_slots) sc.gs = __ldg(a.pool_gs + (int64_t)sc.slot * a.HV + h);
-  }
-  return sc;
-}
-
-// Everything a tile carries from its staging to its store.
-struct TileCtx {
-  TileIdx idx;
-  int64_t pt;    // pool tile index slot * HV + h
-  float c;       // alpha * old global scale
-  float beta;
-  float kq;      // k . q (threads of warps 0..3)
-  float vj;      // v_j (threads of warps 0..3)
-  float k_row;   // k_i of this thread's row
-};
-
 template <int kMode>
-__global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kThreads, 1)
+    gdn_decode_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_codes) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   DecodeSmem& sm = *reinterpret_cast<DecodeSmem*>(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quad = warp & 3;         // TMEM lane subpartition of this warp
-  const int half = warp >> 2;        // which 64 TMEM columns this warp reads
-  const int row = 32 * quad + lane;  // TMEM lane: column j after MMA1', row i after MMA1
+  volatile int* abort_flag = &sm.abort_flag;
+  if ((smem_u32(smem_raw) & 1023u) != 0) {  // the swizzled stages need 1024-byte alignment
+    if (tid == 0) atomicOr(a.status, kStatusWaitTimeout);
+    return;
+  }
 
-  // ---- once per CTA: tables, identity operand, unit scale factors, barriers, TMEM ----
-  sm.inv_tab[tid] = scale_inverse(scale_decode((uint32_t)tid, kMode));
+  // ---- once per CTA: tables, constant operands, barriers, TMEM ----
+  if (tid < 256) sm.inv_tab[tid] = scale_inverse(scale_decode((uint32_t)tid, kMode));
   for (int e = tid; e < (int)kCodeBytes; e += kThreads) {
     const int r = e >> 6, byte = e & 63;
     uint8_t val = 0;
@@ -193,11 +179,22 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const DecodeArg
     if (2 * byte + 1 == r) val = 0x20;  // ... or the high nibble (k = 2 byte + 1)
     sm.ident[canon(r, byte)] = val;
   }
-  reinterpret_cast<uint32_t*>(sm.sf_one)[tid] = 0x38383838u;  // UE4M3 1.0
+  if (tid < 256) reinterpret_cast<uint32_t*>(sm.sf_one)[tid] = 0x38383838u;  // UE4M3 1.0
+  for (int e = tid; e < 2 * kD * 8; e += kThreads) {
+    reinterpret_cast<float*>(sm.ak)[e] = 0.0f;
+    reinterpret_cast<float*>(sm.bw)[e] = 0.0f;
+  }
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&sm.full[s], 1);
-    mbar_init(&sm.bar_dt, 1);
-    mbar_init(&sm.bar_d, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) mbar_init(&sm.bar_t[b], 2);
+    mbar_init(&sm.bar_w, 4);
+    mbar_init(&sm.bar_d, 2);
+    mbar_init(&sm.bar_q, kQWarps);
+    mbar_init(&sm.bar_fin, 1);
+    sm.abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0) tc::tmem_alloc(&sm.tmem_base, kTmemCols);
@@ -206,234 +203,299 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const DecodeArg
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t T = sm.tmem_base;
-  const uint32_t id_mx = tc::idesc_mxf4nvf4(128, 128);
-  const TileIdx first{(int32_t)(blockIdx.x / (uint32_t)a.HV), (int32_t)(blockIdx.x % (uint32_t)a.HV)};
-  TileIdx ahead = first;  // thread 0: the tile whose copies are queued next
-  if (tid == 0) {
-    for (int t = 0; t < 2; ++t) tc::cp_32x128b_warpx4(T + kColOne + 4 * t, tc::smem_desc(sm.sf_one + 512 * t, 0, 128));
-    for (int s = 0; s < kStages; ++s) {
-      if (ahead.b < a.B) issue_tile(a, sm, s, ahead);
-      ahead.advance(a.step_b, a.step_h, a.HV);
-    }
-  }
 
-  bool failed = false;
-  uint32_t par = 0;  // phase of bar_dt / bar_d (one completion per valid tile each)
-  int64_t n = 0;     // local index of the next tile to stage
-  TileIdx sidx = first;             // the next tile to stage
-  TileIdx pidx = first;             // the tile whose scalars are prefetched next
-  Scalars scal = load_scalars(a, pidx);
-  pidx.advance(a.step_b, a.step_h, a.HV);
-
-  // Waits for local tile n, writes zeros for padding tiles, and for the next
-  // valid tile stages its MMA operands, fills `ctx` and issues its MMA1'.
-  // Returns false when this CTA has no tile left (or a wait timed out).
-  auto stage_next = [&](TileCtx& ctx) -> bool {
-    for (;; ++n, sidx.advance(a.step_b, a.step_h, a.HV)) {
-      if (sidx.b >= a.B) return false;
-      const Scalars cur = scal;
-      scal = load_scalars(a, pidx);
-      pidx.advance(a.step_b, a.step_h, a.HV);
-      const int s = (int)(n % kStages);
-      if (!mbar_wait_cta(&sm.full[s], (uint32_t)((n / kStages) & 1))) { failed = true; return false; }
-      const int b = sidx.b, h = sidx.h;
-      if (cur.slot < 0 || cur.slot >= a.num_slots) {
-        __nv_bfloat16* ob = a.out + ((int64_t)b * a.HV + h) * kD;
-        if (tid < kD / 2) reinterpret_cast<uint32_t*>(ob)[tid] = 0u;
-        if (tid == 0) {
-          if (cur.slot >= a.num_slots) atomicOr(a.status, kStatusBadSlot);
-          if (ahead.b < a.B) issue_tile(a, sm, s, ahead);
-          ahead.advance(a.step_b, a.step_h, a.HV);
+  if (warp == kProdWarp) {
+    // =================================== producer ===================================
+    if (lane == 0) {
+      int64_t t = blockIdx.x;
+      int32_t tb = (int32_t)(blockIdx.x / (uint32_t)a.HV), th = (int32_t)(blockIdx.x % (uint32_t)a.HV);
+      const int32_t step_b = (int32_t)(gridDim.x / (uint32_t)a.HV), step_h = (int32_t)(gridDim.x % (uint32_t)a.HV);
+      for (int n = 0;; ++n) {
+        const int s = n % kStages;
+        if (n >= kStages && !wait_bar(&sm.empty[s], (uint32_t)(((n / kStages) - 1) & 1), abort_flag)) break;
+        Stage& st = sm.st[s];
+        // next valid tile (padding tiles: zero output, flag out-of-range slots)
+        int32_t slot = -1;
+        int b = 0, h = 0;
+        while (t < a.ntiles) {
+          b = tb;
+          h = th;
+          slot = __ldg(a.slot_idx + b);
+          t += gridDim.x;
+          th += step_h;
+          tb += step_b;
+          if (th >= a.HV) { th -= a.HV; ++tb; }
+          if (slot >= 0 && slot < a.num_slots) break;
+          uint4* ob = reinterpret_cast<uint4*>(a.out + ((int64_t)b * a.HV + h) * kD);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) ob[e] = make_uint4(0u, 0u, 0u, 0u);
+          if (slot >= a.num_slots) atomicOr(a.status, kStatusBadSlot);
+          slot = -1;
         }
-        continue;
+        TileMeta& m = st.meta;
+        if (slot < 0) {  // walk over: an end marker in this stage
+          m.end = 1;
+          mbar_arrive(&sm.full[s]);
+          break;
+        }
+        const int64_t pt = (int64_t)slot * a.HV + h;
+        const int hk = h / a.group;
+        const float c = expf(__ldg(a.g + (int64_t)b * a.HV + h)) * __ldg(a.pool_gs + pt);
+        m.pt = pt;
+        m.b = b;
+        m.h = h;
+        m.drop = (c >= 0.0f && c < kDropBelow) ? 1 : 0;
+        m.c = m.drop ? 1.0f : c;
+        m.inv_c = 1.0f / m.c;
+        m.beta = __ldg(a.beta + (int64_t)b * a.HV + h);
+        m.end = 0;
+        uint64_t* bar = &sm.full[s];
+        mbar_arrive_expect_tx(bar, kStageTx);  // also publishes the metadata
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+            "[%4];" ::"r"(smem_u32(st.codes)),
+            "l"(&tm_codes), "r"(0), "r"((int32_t)(pt * kD)), "r"(smem_u32(bar))
+            : "memory");
+        bulk_g2s(st.scales, a.pool_scales + pt * kScaleBytes, kScaleBytes, bar);
+        bulk_g2s(st.q, a.q + b * a.q_stride + (int64_t)hk * kD, kVecBytes, bar);
+        bulk_g2s(st.k, a.k + b * a.k_stride + (int64_t)hk * kD, kVecBytes, bar);
+        bulk_g2s(st.v, a.v + b * a.v_stride + (int64_t)h * kD, kVecBytes, bar);
       }
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // ===================================== MMA =====================================
+    const uint32_t id_mx = tc::idesc_mxf4nvf4(128, 128);
+    const uint32_t id_r1 = tc::idesc_tf32(128, 128);
+    if (lane == 0)
+      for (int kt = 0; kt < 2; ++kt) tc::cp_32x128b_warpx4(T + kColOne + 4 * kt, tc::smem_desc(sm.sf_one + 512 * kt, 0, 128));
+    bool ok = true;
+    // Tile n's operands (after its stage landed): scale factors, k/q for the w
+    // warps, then MMA1' into D1'[n & 1].  Returns false at the end marker.
+    auto front = [&](int n, bool& more) -> bool {
+      const int s = n % kStages;
+      if (!wait_bar(&sm.full[s], (uint32_t)((n / kStages) & 1), abort_flag)) return false;
       Stage& st = sm.st[s];
-      ctx.idx = sidx;
-      ctx.pt = (int64_t)cur.slot * a.HV + h;
-      ctx.c = expf(cur.g) * cur.gs;
-      ctx.beta = cur.beta;
-      {
-        // codes -> no-swizzle K-major: thread moves 32 bytes (two 16-byte chunks) of row tid/2
-        const int r = tid >> 1, c0 = 2 * (tid & 1);
-        const uint4* src = reinterpret_cast<const uint4*>(st.codes + r * 64 + 16 * c0);
-        const uint4 x0 = src[0], x1 = src[1];
-        *reinterpret_cast<uint4*>(sm.codes + 2048 * c0 + 16 * r) = x0;
-        *reinterpret_cast<uint4*>(sm.codes + 2048 * (c0 + 1) + 16 * r) = x1;
-        // scale factors: word (t*128 + m0*4 + m1) <- scales of row 32 m1 + m0, blocks 4t..4t+3
-        const int t = tid >> 7, m0 = (tid & 127) >> 2, m1 = tid & 3;
-        reinterpret_cast<uint32_t*>(sm.sf)[t * 128 + m0 * 4 + m1] =
-            reinterpret_cast<const uint32_t*>(st.scales)[(32 * m1 + m0) * 2 + t];
-      }
-      if (tid < kD / 2) {
-        const __nv_bfloat162 k2 = reinterpret_cast<const __nv_bfloat162*>(st.k)[tid];
-        const __nv_bfloat162 q2 = reinterpret_cast<const __nv_bfloat162*>(st.q)[tid];
-        sm.kq4[tid] = make_float4(__low2float(k2), __high2float(k2), __low2float(q2), __high2float(q2));
-      }
-      ctx.k_row = bf2f(st.k[row]);
-      ctx.kq = 0.0f;
-      ctx.vj = 0.0f;
-      if (warp < 4) {
-        float kq = 0.0f;
+      more = !st.meta.end;
+      if (!more) return true;
+      uint32_t* sfw = reinterpret_cast<uint32_t*>(sm.sfb[n & 1]);
+      const uint32_t* scw = reinterpret_cast<const uint32_t*>(st.scales);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) kq = fmaf(bf2f(st.k[4 * lane + i]), bf2f(st.q[4 * lane + i]), kq);
+      for (int r = 0; r < 8; ++r) {
+        const int qd = lane + 32 * r;
+        const int t = qd >> 7, m0 = (qd & 127) >> 2, m1 = qd & 3;
+        sfw[t * 128 + m0 * 4 + m1] = scw[(32 * m1 + m0) * 2 + t];
+      }
+      float kq = 0.0f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) kq += __shfl_xor_sync(0xffffffffu, kq, o);
-        ctx.kq = kq;
-        ctx.vj = bf2f(st.v[tid]);
+      for (int r = 0; r < 2; ++r) {
+        const int i2 = lane + 32 * r;  // pair (2 i2, 2 i2 + 1)
+        const __nv_bfloat162 k2 = reinterpret_cast<const __nv_bfloat162*>(st.k)[i2];
+        const __nv_bfloat162 q2 = reinterpret_cast<const __nv_bfloat162*>(st.q)[i2];
+        const float4 f = make_float4(__low2float(k2), __high2float(k2), __low2float(q2), __high2float(q2));
+        sm.kq4[n & 1][i2] = f;
+        kq = fmaf(f.x, f.z, fmaf(f.y, f.w, kq));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) kq += __shfl_xor_sync(0xffffffffu, kq, o);
+      // D1'[n & 1] was last read by the w warps for tile n - 2 (bar_w waited since)
+      tc::fence_smem_to_async();
+      __syncwarp();
+      if (lane == 0) {
+        InfoW& iw = sm.iw[n & 1];
+        iw.m = st.meta;
+        iw.kq = kq;
+        iw.stage = s;
+        const uint32_t sf = T + kColSF + 8 * (n % 3);
+        for (int kt = 0; kt < 2; ++kt) tc::cp_32x128b_warpx4(sf + 4 * kt, tc::smem_desc(sm.sfb[n & 1] + 512 * kt, 0, 128));
+        for (int kt = 0; kt < 2; ++kt)
+          tc::mma_mxf4nvf4(T + kColD1t + 128 * (n & 1), tc::smem_desc(sm.ident + 4096 * kt, 2048, 128),
+                           desc_codes(st.codes, kt), id_mx, T + kColOne + 4 * kt, sf + 4 * kt, kt > 0);
+        mbar_arrive(&sm.bar_t[n & 1]);  // publishes iw, kq4
+        tc::commit(&sm.bar_t[n & 1]);
+      }
+      __syncwarp();
+      return true;
+    };
+    bool more = true;
+    ok = front(0, more);
+    int n = 0;
+    for (; ok && more; ++n) {
+      const int s = n % kStages;
+      Stage& st = sm.st[s];
+      // tile n + 1's decode goes ahead of tile n's update (D1'[(n + 1) & 1] is
+      // free: the w warps finished tile n - 1, waited for in the last iteration)
+      bool more_next = false;
+      if (!front(n + 1, more_next)) { ok = false; break; }
+      // MMA1(n) + MMA_r1(n) into D1 once w(n) is ready and the requantisers read D1 (tile n - 1)
+      if (!wait_bar(&sm.bar_w, (uint32_t)(n & 1), abort_flag)) { ok = false; break; }
+      if (n >= 1 && !wait_bar(&sm.bar_q, (uint32_t)((n - 1) & 1), abort_flag)) { ok = false; break; }
+      tc::fence_after_sync();
+      uint8_t* ak = sm.ak[n & 1];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int i = lane + 32 * r;
+        const float kv = bf2f(st.k[i]);
+        *reinterpret_cast<float*>(ak + kf32(i, 0, 256)) = kv;
+        *reinterpret_cast<float*>(ak + kf32(i, 1, 256)) = kv;
       }
       tc::fence_smem_to_async();
-      tc::fence_before_sync();
-      __syncthreads();  // operands staged, stage s consumed
+      __syncwarp();
+      if (lane == 0) {
+        sm.iq = st.meta;
+        const uint32_t sf = T + kColSF + 8 * (n % 3);
+        if (!st.meta.drop)
+          for (int kt = 0; kt < 2; ++kt)
+            tc::mma_mxf4nvf4(T + kColD1, desc_codes(st.codes, kt), tc::smem_desc(sm.ident + 4096 * kt, 2048, 128),
+                             id_mx, sf + 4 * kt, T + kColOne + 4 * kt, kt > 0);
+        tc::mma_tf32_ss(T + kColD1, tc::smem_desc(ak, 128, 256), tc::smem_desc(sm.bw[n & 1], 128, 256), id_r1,
+                        st.meta.drop ? 0u : 1u);
+        mbar_arrive(&sm.bar_d);  // publishes iq
+        tc::commit(&sm.bar_d);
+        tc::commit(&sm.empty[s]);
+      }
+      __syncwarp();
+      more = more_next;
+    }
+    // end: tell the w and requantiser warps (n = number of tiles)
+    if (ok) {
+      const int N = n;
+      // w warps: an end marker in iw[N & 1] (they finished tile N - 2: bar_w(N - 1) seen)
+      if (lane == 0) {
+        sm.iw[N & 1].m.end = 1;
+        mbar_arrive(&sm.bar_t[N & 1]);
+        mbar_arrive(&sm.bar_t[N & 1]);
+      }
+      if (N >= 1) ok = wait_bar(&sm.bar_q, (uint32_t)((N - 1) & 1), abort_flag);
+      if (ok && lane == 0) {
+        sm.iq.end = 1;
+        mbar_arrive(&sm.bar_d);
+        mbar_arrive(&sm.bar_d);
+      }
+    }
+    if (!ok) *abort_flag = 1;
+    // every tcgen05 operation this warp issued has completed before TMEM is freed
+    if (lane == 0) {
+      tc::commit(&sm.bar_fin);
+      mbar_wait_bounded(&sm.bar_fin, 0, kWaitTimeoutNs / 4);
+    }
+    __syncwarp();
+  } else if (warp >= kWWarp0) {
+    // ================================ w and outputs ================================
+    const int j = 32 * (warp & 3) + lane;
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    for (int n = 0;; ++n) {
+      if (!wait_bar(&sm.bar_t[n & 1], (uint32_t)((n >> 1) & 1), abort_flag)) break;
+      const InfoW iw = sm.iw[n & 1];
+      if (iw.m.end) break;
       tc::fence_after_sync();
-      if (tid == 0) {
-        if (ahead.b < a.B) issue_tile(a, sm, s, ahead);
-        ahead.advance(a.step_b, a.step_h, a.HV);
-        // MMA1': D = I * S^T (lane j, column i)
-        for (int t = 0; t < 2; ++t) tc::cp_32x128b_warpx4(T + kColSF + 4 * t, tc::smem_desc(sm.sf + 512 * t, 0, 128));
-        for (int t = 0; t < 2; ++t)
-          tc::mma_mxf4nvf4(T + kColD, tc::smem_desc(sm.ident + 4096 * t, 2048, 128),
-                           tc::smem_desc(sm.codes + 4096 * t, 2048, 128), id_mx, T + kColOne + 4 * t,
-                           T + kColSF + 4 * t, t > 0);
-        tc::commit(&sm.bar_dt);
-      }
-      ++n;
-      sidx.advance(a.step_b, a.step_h, a.HV);
-      return true;
-    }
-  };
-
-  TileCtx cur, nxt;
-  bool have = stage_next(cur);
-  while (have) {
-    const int b = cur.idx.b, h = cur.idx.h;
-    __nv_bfloat16* ob = a.out + ((int64_t)b * a.HV + h) * kD;
-
-    // ---- 1: the transposed tile -> partial S^T k, S^T q over this thread's 64 rows ----
-    if (!mbar_wait_cta(&sm.bar_dt, par)) { failed = true; break; }
-    tc::fence_after_sync();
-    float2 x[32];
-    {
-      const uint32_t ta = T + ((uint32_t)(32 * quad) << 16) + kColD + 64 * half;
-      tc::ld_32x32b_x32(ta, reinterpret_cast<float*>(x));
-      tc::ld_32x32b_x32(ta + 32, reinterpret_cast<float*>(x) + 32);
-      tc::ld_wait();
-    }
-    tc::fence_before_sync();
-    __syncthreads();  // D read by every thread: MMA1 may overwrite it
-    tc::fence_after_sync();
-    if (tid == 0) {
-      // MMA1: D = S * I (lane i, column j)
-      for (int t = 0; t < 2; ++t)
-        tc::mma_mxf4nvf4(T + kColD, tc::smem_desc(sm.codes + 4096 * t, 2048, 128),
-                         tc::smem_desc(sm.ident + 4096 * t, 2048, 128), id_mx, T + kColSF + 4 * t,
-                         T + kColOne + 4 * t, t > 0);
-      tc::commit(&sm.bar_d);
-    }
-    {
-      // x[p] = (S[64 half + 2p][j], S[64 half + 2p + 1][j]) * scale (unscaled by c)
+      // u / c, p / c = row j of D1' against k, q
       float2 su = make_float2(0.0f, 0.0f), sp = make_float2(0.0f, 0.0f);
-      const float4* kq4 = sm.kq4 + 32 * half;
+      const float4* kq4 = sm.kq4[n & 1];
 #pragma unroll
-      for (int p = 0; p < 32; ++p) {
-        const float4 kq = kq4[p];
-        su = __ffma2_rn(x[p], make_float2(kq.x, kq.y), su);
-        sp = __ffma2_rn(x[p], make_float2(kq.z, kq.w), sp);
+      for (int c32 = 0; c32 < 4; ++c32) {
+        float2 x[16];
+        tc::ld_32x32b_x32(T + lane_base + kColD1t + 128 * (n & 1) + 32 * c32, reinterpret_cast<float*>(x));
+        tc::ld_wait();
+#pragma unroll
+        for (int p = 0; p < 16; ++p) {
+          const float4 kq = kq4[16 * c32 + p];
+          su = __ffma2_rn(x[p], make_float2(kq.x, kq.y), su);
+          sp = __ffma2_rn(x[p], make_float2(kq.z, kq.w), sp);
+        }
       }
-      sm.red[half][0][row] = su.x + su.y;
-      sm.red[half][1][row] = sp.x + sp.y;
-    }
-    __syncthreads();  // partial sums of both row halves published
-    if (warp < 4) {
-      const int j = tid;
-      const float u = cur.c * (sm.red[0][0][j] + sm.red[1][0][j]);
-      const float pq = cur.c * (sm.red[0][1][j] + sm.red[1][1][j]);
-      const float wj = cur.beta * (cur.vj - u);
-      sm.w[j] = wj;
-      const float o0 = a.q_scale * fmaf(cur.kq, wj, pq);
-      const float o1 = __shfl_down_sync(0xffffffffu, o0, 1);
+      tc::fence_before_sync();
+      const TileMeta& m = iw.m;
+      const float c = m.drop ? 0.0f : m.c;
+      const float u = su.x + su.y, p = sp.x + sp.y;
+      const float vj = bf2f(sm.st[iw.stage].v[j]);
+      const float wj = m.beta * (vj - c * u);
+      const float o = a.q_scale * fmaf(iw.kq, wj, c * p);
+      const float o1 = __shfl_down_sync(0xffffffffu, o, 1);
       if ((j & 1) == 0)
-        reinterpret_cast<uint32_t*>(ob)[j >> 1] = (uint32_t)f2bf_bits(o0) | ((uint32_t)f2bf_bits(o1) << 16);
+        reinterpret_cast<uint32_t*>(a.out + ((int64_t)m.b * a.HV + m.h) * kD)[j >> 1] =
+            (uint32_t)f2bf_bits(o) | ((uint32_t)f2bf_bits(o1) << 16);
+      const float wc = wj * m.inv_c;
+      const float hi = __uint_as_float(__float_as_uint(wc) & 0xFFFFE000u);
+      uint8_t* bw = sm.bw[n & 1];
+      *reinterpret_cast<float*>(bw + kf32(j, 0, 256)) = hi;
+      *reinterpret_cast<float*>(bw + kf32(j, 1, 256)) = wc - hi;
+      tc::fence_smem_to_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.bar_w);
     }
-
-    // ---- 2: the tile (lane i) -> registers ----
-    const bool ok_d = mbar_wait_cta(&sm.bar_d, par);  // also publishes w
-    par ^= 1;
-    if (!ok_d) { failed = true; break; }
-    tc::fence_after_sync();
-    {
-      const uint32_t ta = T + ((uint32_t)(32 * quad) << 16) + kColD + 64 * half;
-      tc::ld_32x32b_x32(ta, reinterpret_cast<float*>(x));
-      tc::ld_32x32b_x32(ta + 32, reinterpret_cast<float*>(x) + 32);
-      tc::ld_wait();
-    }
-    tc::fence_before_sync();
-
-    // ---- 3: stage the next tile and start its MMA1' (overlaps 4-5) ----
-    have = stage_next(nxt);
-
-    // ---- 4: rank-1 update of this thread's row, block and tile amax ----
-    const float2 c2 = make_float2(cur.c, cur.c), k2 = make_float2(cur.k_row, cur.k_row);
-    const float4* w4 = reinterpret_cast<const float4*>(sm.w + 64 * half);  // w of this thread's columns
-    float am[4];
-    float tmax = 0.0f;
-#pragma unroll
-    for (int blk = 0; blk < 4; ++blk) {
-      float mx = 0.0f;
-#pragma unroll
-      for (int p = 0; p < 8; p += 2) {
-        const float4 wv = w4[4 * blk + p / 2];
-        float2& v0 = x[8 * blk + p];
-        float2& v1 = x[8 * blk + p + 1];
-        v0 = __ffma2_rn(k2, make_float2(wv.x, wv.y), __fmul2_rn(v0, c2));
-        v1 = __ffma2_rn(k2, make_float2(wv.z, wv.w), __fmul2_rn(v1, c2));
-        mx = (p == 0) ? absmax_nan(v0.x, v0.y) : absmax_nan(absmax_nan(mx, v0.x), v0.y);
-        mx = absmax_nan(absmax_nan(mx, v1.x), v1.y);
+  } else {
+    // ================================ requantisation ================================
+    const int quad = warp & 3, half = warp >> 2;
+    const int row = 32 * quad + lane;  // TMEM lane = state row i
+    const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
+    for (int n = 0;; ++n) {
+      if (!wait_bar(&sm.bar_d, (uint32_t)(n & 1), abort_flag)) break;
+      const TileMeta m = sm.iq;
+      if (m.end) break;
+      tc::fence_after_sync();
+      float2 x[32];
+      {
+        const uint32_t ta = T + lane_base + kColD1 + 64 * half;
+        tc::ld_32x32b_x32(ta, reinterpret_cast<float*>(x));
+        tc::ld_32x32b_x32(ta + 32, reinterpret_cast<float*>(x) + 32);
+        tc::ld_wait();
       }
-      am[blk] = fabsf(mx);
-      float ok_max = am[blk];
-      if (isnan(ok_max)) {  // rare: the reference's amax ignores NaN
-        ok_max = 0.0f;
+      // D1 and iq are read: release them to the MMA warp
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.bar_q);
+      // block abs-max: three-input max, NaN-propagating (a NaN block takes the exact path)
+      float am[4];
+      float tmax = 0.0f;
 #pragma unroll
-        for (int p = 0; p < 8; ++p) ok_max = fmaxf(ok_max, fmaxf(fabsf(x[8 * blk + p].x), fabsf(x[8 * blk + p].y)));
+      for (int blk = 0; blk < 4; ++blk) {
+        const float2* xb = x + 8 * blk;
+        float m0, m1;
+        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(xb[0].x), "f"(xb[0].y), "f"(xb[1].x));
+        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m1) : "f"(xb[1].y), "f"(xb[2].x), "f"(xb[2].y));
+        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(m0), "f"(xb[3].x), "f"(xb[3].y));
+        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m1) : "f"(m1), "f"(xb[4].x), "f"(xb[4].y));
+        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(m0), "f"(xb[5].x), "f"(xb[5].y));
+        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m1) : "f"(m1), "f"(xb[6].x), "f"(xb[6].y));
+        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(m0), "f"(xb[7].x), "f"(xb[7].y));
+        float mb;
+        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(mb) : "f"(m0), "f"(m1), "f"(0.0f));
+        am[blk] = mb;
+        float ok_max = mb;
+        if (isnan(mb)) {  // rare: the reference's amax ignores NaN
+          ok_max = 0.0f;
+#pragma unroll
+          for (int p = 0; p < 8; ++p) ok_max = fmaxf(ok_max, fmaxf(fabsf(xb[p].x), fabsf(xb[p].y)));
+        }
+        tmax = fmaxf(tmax, ok_max);
       }
-      tmax = fmaxf(tmax, ok_max);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+      if (lane == 0) sm.amax[n & 1][warp] = tmax;
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight requantiser warps
+      float amax = sm.amax[n & 1][0];
+#pragma unroll
+      for (int w = 1; w < kQWarps; ++w) amax = fmaxf(amax, sm.amax[n & 1][w]);
+      // S' = c D1: gs' = amax(S') / gden; y = D1 (c / gs')
+      const float amax_s = m.c * amax;
+      const float gs_new = (amax_s > 0.0f) ? __fdiv_rn(amax_s, a.gden) : 1.0f;
+      const float mult = __fmul_rn(m.c, __frcp_rn(gs_new));
+      uint32_t words[8], scw;
+      requant_half_row<kMode>(
+          x, am, mult, sm.inv_tab, words, scw,
+          a.debug_y ? a.debug_y + (((int64_t)m.b * a.HV + m.h) * kD + row) * kD + 64 * half : nullptr);
+      uint4* dst = reinterpret_cast<uint4*>(a.pool_codes + m.pt * kCodeBytes + row * 64 + 32 * half);
+      dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
+      dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
+      *reinterpret_cast<uint32_t*>(a.pool_scales + m.pt * kScaleBytes + row * 8 + 4 * half) = scw;
+      if (tid == 0) a.pool_gs[m.pt] = gs_new;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
-    if (lane == 0) sm.amax[warp] = tmax;
-    __syncthreads();  // tile amax
-    float amax = sm.amax[0];
-#pragma unroll
-    for (int w = 1; w < kWarps; ++w) amax = fmaxf(amax, sm.amax[w]);
-    const float gs_new = (amax > 0.0f) ? __fdiv_rn(amax, a.gden) : 1.0f;
-    const float inv_gs = __frcp_rn(gs_new);
-
-    // ---- 5: requantise this thread's four blocks, store ----
-    uint32_t words[8];
-    uint32_t scw;
-    requant_half_row<kMode>(x, am, inv_gs, sm.inv_tab, words, scw,
-                            a.debug_y ? a.debug_y + (((int64_t)b * a.HV + h) * kD + row) * kD + 64 * half : nullptr);
-    uint4* dst = reinterpret_cast<uint4*>(a.pool_codes + cur.pt * kCodeBytes + row * 64 + 32 * half);
-    dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
-    dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
-    *reinterpret_cast<uint32_t*>(a.pool_scales + cur.pt * kScaleBytes + row * 8 + 4 * half) = scw;
-    if (tid == 0) a.pool_gs[cur.pt] = gs_new;
-    cur = nxt;
   }
 
-  if (failed && tid == 0) {
-    // Report, then give the copies this CTA queued a bounded chance to land
-    // before its shared memory is released.
-    atomicOr(a.status, kStatusWaitTimeout);
-    // local tiles n .. n + kStages - 1 may have copies queued
-    TileIdx t = sidx;
-    for (int64_t m = n; m < n + kStages; ++m, t.advance(a.step_b, a.step_h, a.HV)) {
-      if (t.b >= a.B) break;
-      mbar_wait_bounded(&sm.full[m % kStages], (uint32_t)((m / kStages) & 1), kWaitTimeoutNs / 4);
-    }
-  }
-  // Every tcgen05 operation of this CTA has been waited on (or abandoned after
-  // a timeout); release the tensor memory.
+  if (*abort_flag && tid == 0) atomicOr(a.status, kStatusWaitTimeout);
+  // Every tcgen05 operation has completed (or was abandoned after a timeout);
+  // release the tensor memory.
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -444,6 +506,23 @@ __global__ void __launch_bounds__(kThreads, 2) gdn_decode_kernel(const DecodeArg
 }  // namespace gdn
 
 using namespace gdn;
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+}  // namespace
 
 extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
   if (!p) return GDN_ERR_ARGS;
@@ -473,6 +552,8 @@ extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
       !aligned16(p->pool_scales) || !aligned16(p->out) || (a.q_stride | a.k_stride | a.v_stride) % 8 ||
       (p->debug_y && !aligned16(p->debug_y)))
     return GDN_ERR_ALIGN;
+  // The codes are addressed as rows of a 2-D tensor map (int32 row coordinate).
+  if (a.ntiles > INT32_MAX || p->num_slots * (int64_t)p->num_v_heads * kD > INT32_MAX) return GDN_ERR_UNSUPPORTED;
   a.g = p->g;
   a.beta = p->beta;
   a.slot_idx = p->slot_idx;
@@ -488,12 +569,24 @@ extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
   a.status = device_status_ptr();
   if (!a.status) return GDN_ERR_CUDA;
 
+  CUtensorMap tm;
+  {
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return GDN_ERR_CUDA;
+    const int64_t rows = p->num_slots > 0 ? p->num_slots * (int64_t)p->num_v_heads * kD : kD;
+    const cuuint64_t dims[2] = {64, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {64};
+    const cuuint32_t box[2] = {64, kD};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p->pool_codes, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return GDN_ERR_CUDA;
+  }
+
   const int smem = (int)sizeof(DecodeSmem);
-  const int64_t max_ctas = (int64_t)sm_count() * 2;
+  const int64_t max_ctas = sm_count();
   const int grid = (int)(a.ntiles < max_ctas ? a.ntiles : max_ctas);
-  if (a.ntiles > INT32_MAX) return GDN_ERR_UNSUPPORTED;
-  a.step_b = grid / a.HV;
-  a.step_h = grid % a.HV;
   // Opt in to > 48 KB of dynamic shared memory once per device and kernel.
   static bool attr_set[2][64] = {};
   int dev = 0;
@@ -508,8 +601,8 @@ extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
     attr_set[mi][dev] = true;
   }
   if (mi == 0)
-    gdn_decode_kernel<kScaleRef240><<<grid, kThreads, smem, stream>>>(a);
+    gdn_decode_kernel<kScaleRef240><<<grid, kThreads, smem, stream>>>(a, tm);
   else
-    gdn_decode_kernel<kScaleFn448><<<grid, kThreads, smem, stream>>>(a);
+    gdn_decode_kernel<kScaleFn448><<<grid, kThreads, smem, stream>>>(a, tm);
   return launch_status();
 }
