@@ -15,23 +15,25 @@
 // The decode and the rank-1 update run on the tensor cores.  With
 // c = alpha gs and S_dq = e2m1 * block scale (so S = gs S_dq):
 //   MMA1'   D1' = I * S_dq^T          block-scaled E2M1 MMA against an identity
-//                                     (lane = column j; double-buffered)
-//   SIMT    [u p] / c = D1' [k q]     each w thread reduces its own row of D1'
-//   MMA1    D1  = S_dq * I            the tile again, lane = row i
+//                                     (lane = column j)
+//   SIMT    [u p] / c = D1' [k q]     each w thread reduces half a row of D1'
+//   MMA1    D1  = S_dq * I            the tile again, lane = row i (double-buffered)
 //   MMA_r1  D1 += k (w / c)^T         tf32 rank-1 update, w / c split hi + lo
-// so S' = c D1 and the requantiser reads y = D1 * (c / gs') straight from TMEM.
-// The codes arrive by one 2-D TMA copy with 64-byte swizzle that both decode
-// MMAs read in place.
+// so S' = c D1 and the requantiser reads y = D1 * (c / gs') straight from
+// TMEM, in two passes (block maxima, then quantisation) so that a thread never
+// holds more than 32 values.  The codes arrive by one 2-D TMA copy with 64-byte
+// swizzle that both decode MMAs read in place.
 //
-// Warp roles (one CTA per SM, 14 warps):
-//   warp 13     producer: walks the CTA's tiles, loads the per-tile scalars,
-//               queues the TMA copies into a 6-stage ring, zeroes the outputs
-//               of padding tiles;
-//   warp 12     MMA: scale-factor permutation, the [k q] operand, every MMA
-//               and commit; it issues tile n+1's MMA1' before waiting for
-//               tile n's w;
-//   warps 8-11  w: u, p -> w, o (stored) and the rank-1 operand;
-//   warps 0-7   requantise D1 and store the tile.
+// Warp roles (one CTA per SM, 27 warps):
+//   warp 25     producer: walks the CTA's tiles, loads the per-tile scalars
+//               into a metadata ring, queues the TMA copies into a 6-stage
+//               ring, zeroes the outputs of padding tiles;
+//   warp 26     staging: once a stage lands, permutes its scale factors into
+//               the tcgen05.cp layout and writes the fp32 k / q operands;
+//   warp 24     MMA: only tcgen05 work -- every copy, MMA and commit; it
+//               issues tile n+1's MMA1' before tile n's update;
+//   warps 16-23 w: u, p -> w, o (stored) and the rank-1 operand;
+//   warps 0-15  requantisers, two groups of 8 taking alternate tiles.
 // Every wait is bounded; a timeout in any role stops all of them.
 #include <cstdint>
 #include <mutex>
@@ -48,22 +50,27 @@ namespace gdn {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kQWarps = 8;
-constexpr int kWWarp0 = 8;
-constexpr int kMmaWarp = 12;
-constexpr int kProdWarp = 13;
-constexpr int kThreads = 14 * 32;
+constexpr int kQWarps = 16;  // two groups of 8
+constexpr int kWWarp0 = 16;  // 8 w warps
+constexpr int kMmaWarp = 24;
+constexpr int kProdWarp = 25;
+constexpr int kStageWarp = 26;
+constexpr int kThreads = 27 * 32;
 constexpr int kStages = 6;
+constexpr int kRing = 16;  // metadata ring entries
 constexpr uint32_t kCodeBytes = kD * kD / 2;    // 8192
 constexpr uint32_t kScaleBytes = kD * kD / 16;  // 1024
 constexpr uint32_t kVecBytes = kD * 2;          // 256
 constexpr uint32_t kStageTx = kCodeBytes + kScaleBytes + 3 * kVecBytes;
 constexpr float kDropBelow = 1e-30f;            // alpha * gs below this: the decayed state is zero
 
+// Named hardware barriers (0 is __syncthreads)
+constexpr int kBarQ0 = 1, kBarQ1 = 3, kBarW = 2;
+
 // TMEM columns (512 allocated)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColD1 = 0;     // 128: D1 (lane i)
-constexpr uint32_t kColD1t = 128;  // 2 x 128: D1' (lane j), double-buffered
+constexpr uint32_t kColD1 = 0;     // 2 x 128: D1 (lane i), one per requantiser group
+constexpr uint32_t kColD1t = 256;  // 128: D1' (lane j)
 constexpr uint32_t kColSF = 384;   // 3 x 8: the tile's scale factors (tile n uses n % 3: the
                                    // slot is rewritten only after tile n - 3's MMA1 is known complete)
 constexpr uint32_t kColOne = 408;  // 8: unit scale factors of the identity
@@ -74,6 +81,7 @@ struct TileMeta {
   float c;          // alpha * gs (1 when the decayed state is dropped)
   float inv_c;
   float beta;
+  float kq;         // k . q
   int32_t drop;     // alpha * gs < kDropBelow: S_a = 0
   int32_t end;      // no more tiles
 };
@@ -84,28 +92,22 @@ struct __align__(1024) Stage {
   __nv_bfloat16 q[kD];
   __nv_bfloat16 k[kD];
   __nv_bfloat16 v[kD];
-  TileMeta meta;
-};
-
-struct InfoW {
-  TileMeta m;
-  float kq;
-  int32_t stage;
+  uint8_t sfp[kScaleBytes];   // scale factors in the tcgen05.cp 32x128b layout, 2 K-steps
+  float4 kq4[kD / 2];         // (k_i, k_i+1, q_i, q_i+1), even i
+  uint8_t ak[kD * 8 * 4];     // [128][8] fp32 K-major: columns 0, 1 = k, the rest 0
 };
 
 struct __align__(1024) DecodeSmem {
   Stage st[kStages];
   uint8_t ident[kCodeBytes];  // identity, no-swizzle K-major: byte b of row r at (b % 16) + 16 r + 2048 (b / 16)
   uint8_t sf_one[kScaleBytes];
-  uint8_t sfb[2][kScaleBytes];  // tcgen05.cp 32x128b layout, 2 K-steps
-  float4 kq4[2][kD / 2];        // (k_i, k_i+1, q_i, q_i+1), even i
-  uint8_t ak[2][kD * 8 * 4];    // [128][8] fp32 K-major: columns 0, 1 = k
   uint8_t bw[2][kD * 8 * 4];    // [128][8] fp32 K-major: columns 0, 1 = hi, lo of w / c
-  InfoW iw[2];
-  TileMeta iq;
-  float amax[2][kQWarps];
+  float2 red[kD];               // partial [u p] / c of the second half of each row of D1'
+  TileMeta ring[kRing];         // metadata of valid tile n at n % kRing
+  uint32_t amax_bits[2][2];     // per group, per tile parity: tile max |D1| as float bits
   float inv_tab[256];
-  uint64_t full[kStages], empty[kStages], bar_t[2], bar_w, bar_d, bar_q, bar_fin;
+  uint64_t full[kStages], ready[kStages], empty[kStages];
+  uint64_t bar_t, bar_tfree, bar_w[2], bar_d[2], bar_q[2], bar_fin;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -118,6 +120,9 @@ __device__ __forceinline__ uint32_t kf32(int row, int k, uint32_t sbo) {
 __device__ __forceinline__ uint64_t desc_codes(const uint8_t* codes, int kstep) {
   // K-major, 64-byte swizzle: 8-row groups 512 bytes apart, K step = 32 bytes (64 E2M1 values)
   return tc::smem_desc(codes + 32 * kstep, 16, 512) | (4ull << 61);
+}
+__device__ __forceinline__ void named_bar(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 struct DecodeArgs {
@@ -180,19 +185,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     sm.ident[canon(r, byte)] = val;
   }
   if (tid < 256) reinterpret_cast<uint32_t*>(sm.sf_one)[tid] = 0x38383838u;  // UE4M3 1.0
-  for (int e = tid; e < 2 * kD * 8; e += kThreads) {
-    reinterpret_cast<float*>(sm.ak)[e] = 0.0f;
-    reinterpret_cast<float*>(sm.bw)[e] = 0.0f;
-  }
+  for (int e = tid; e < 2 * kD * 8; e += kThreads) reinterpret_cast<float*>(sm.bw)[e] = 0.0f;
+  for (int e = tid; e < kStages * kD * 8; e += kThreads)
+    reinterpret_cast<float*>(sm.st[e / (kD * 8)].ak)[e % (kD * 8)] = 0.0f;
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.ready[s], 1);
       mbar_init(&sm.empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) mbar_init(&sm.bar_t[b], 2);
-    mbar_init(&sm.bar_w, 4);
-    mbar_init(&sm.bar_d, 2);
-    mbar_init(&sm.bar_q, kQWarps);
+    mbar_init(&sm.bar_t, 2);
+    mbar_init(&sm.bar_tfree, 8);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.bar_w[b], 4);   // per tile parity: tile n + 1 may finish before tile n is waited for
+      mbar_init(&sm.bar_d[b], 2);   // per requantiser group
+      mbar_init(&sm.bar_q[b], 8);
+      sm.amax_bits[b][0] = sm.amax_bits[b][1] = 0u;
+    }
     mbar_init(&sm.bar_fin, 1);
     sm.abort_flag = 0;
     fence_mbar_init();
@@ -206,63 +215,135 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProdWarp) {
     // =================================== producer ===================================
-    if (lane == 0) {
-      int64_t t = blockIdx.x;
-      int32_t tb = (int32_t)(blockIdx.x / (uint32_t)a.HV), th = (int32_t)(blockIdx.x % (uint32_t)a.HV);
-      const int32_t step_b = (int32_t)(gridDim.x / (uint32_t)a.HV), step_h = (int32_t)(gridDim.x % (uint32_t)a.HV);
-      for (int n = 0;; ++n) {
+    // Lane l loads the scalars of tile t0 + l * gridDim.x for a batch of 32
+    // tiles at a time (the next batch's loads are in flight while this one is
+    // queued), so the dependent slot -> global-scale loads cost one latency
+    // per 32 tiles; lane 0 queues the copies in tile order.
+    struct Scal {
+      int64_t pt;
+      int32_t b, h, slot;
+      float c, beta;
+      int32_t live;  // tile index < ntiles
+    };
+    auto load_batch = [&](int64_t tb0) -> Scal {
+      Scal r{0, 0, 0, -1, 0.0f, 0.0f, 0};
+      const int64_t t = tb0 + (int64_t)lane * gridDim.x;
+      if (t < a.ntiles) {
+        r.live = 1;
+        r.b = (int32_t)(t / a.HV);
+        r.h = (int32_t)(t - (int64_t)r.b * a.HV);
+        r.slot = __ldg(a.slot_idx + r.b);
+        if (r.slot >= 0 && r.slot < a.num_slots) {
+          r.pt = (int64_t)r.slot * a.HV + r.h;
+          const int64_t gi = (int64_t)r.b * a.HV + r.h;
+          r.c = expf(__ldg(a.g + gi)) * __ldg(a.pool_gs + r.pt);
+          r.beta = __ldg(a.beta + gi);
+        }
+      }
+      return r;
+    };
+    int64_t tb0 = blockIdx.x;
+    const int64_t batch_step = 32ll * gridDim.x;
+    Scal cur = load_batch(tb0);
+    int n = 0;
+    bool done = false, ok = true;
+    while (!done && ok) {
+      const Scal nxt = load_batch(tb0 + batch_step);
+      for (int l = 0; l < 32; ++l) {
+        const int live = __shfl_sync(0xffffffffu, cur.live, l);
+        if (!live) { done = true; break; }
+        const int32_t slot = __shfl_sync(0xffffffffu, cur.slot, l);
+        const int32_t b = __shfl_sync(0xffffffffu, cur.b, l);
+        const int32_t h = __shfl_sync(0xffffffffu, cur.h, l);
+        if (slot < 0 || slot >= a.num_slots) {  // padding: zero output, flag out-of-range slots
+          reinterpret_cast<uint2*>(a.out + ((int64_t)b * a.HV + h) * kD)[lane] = make_uint2(0u, 0u);
+          if (lane == 0 && slot >= a.num_slots) atomicOr(a.status, kStatusBadSlot);
+          continue;
+        }
+        const int64_t pt = __shfl_sync(0xffffffffu, cur.pt, l);
+        const float c = __shfl_sync(0xffffffffu, cur.c, l);
+        const float beta = __shfl_sync(0xffffffffu, cur.beta, l);
         const int s = n % kStages;
-        if (n >= kStages && !wait_bar(&sm.empty[s], (uint32_t)(((n / kStages) - 1) & 1), abort_flag)) break;
-        Stage& st = sm.st[s];
-        // next valid tile (padding tiles: zero output, flag out-of-range slots)
-        int32_t slot = -1;
-        int b = 0, h = 0;
-        while (t < a.ntiles) {
-          b = tb;
-          h = th;
-          slot = __ldg(a.slot_idx + b);
-          t += gridDim.x;
-          th += step_h;
-          tb += step_b;
-          if (th >= a.HV) { th -= a.HV; ++tb; }
-          if (slot >= 0 && slot < a.num_slots) break;
-          uint4* ob = reinterpret_cast<uint4*>(a.out + ((int64_t)b * a.HV + h) * kD);
-#pragma unroll
-          for (int e = 0; e < 16; ++e) ob[e] = make_uint4(0u, 0u, 0u, 0u);
-          if (slot >= a.num_slots) atomicOr(a.status, kStatusBadSlot);
-          slot = -1;
+        if (lane == 0) {
+          if (n >= kStages && !wait_bar(&sm.empty[s], (uint32_t)(((n / kStages) - 1) & 1), abort_flag)) ok = false;
+          if (ok) {
+            Stage& st = sm.st[s];
+            TileMeta& m = sm.ring[n % kRing];
+            m.pt = pt;
+            m.b = b;
+            m.h = h;
+            m.drop = (c >= 0.0f && c < kDropBelow) ? 1 : 0;
+            m.c = m.drop ? 1.0f : c;
+            m.inv_c = 1.0f / m.c;
+            m.beta = beta;
+            m.end = 0;
+            const int hk = h / a.group;
+            uint64_t* bar = &sm.full[s];
+            mbar_arrive_expect_tx(bar, kStageTx);  // also publishes the metadata
+            asm volatile(
+                "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+                "%3}], [%4];" ::"r"(smem_u32(st.codes)),
+                "l"(&tm_codes), "r"(0), "r"((int32_t)(pt * kD)), "r"(smem_u32(bar))
+                : "memory");
+            bulk_g2s(st.scales, a.pool_scales + pt * kScaleBytes, kScaleBytes, bar);
+            bulk_g2s(st.q, a.q + b * a.q_stride + (int64_t)hk * kD, kVecBytes, bar);
+            bulk_g2s(st.k, a.k + b * a.k_stride + (int64_t)hk * kD, kVecBytes, bar);
+            bulk_g2s(st.v, a.v + b * a.v_stride + (int64_t)h * kD, kVecBytes, bar);
+          }
         }
-        TileMeta& m = st.meta;
-        if (slot < 0) {  // walk over: an end marker in this stage
-          m.end = 1;
-          mbar_arrive(&sm.full[s]);
-          break;
-        }
-        const int64_t pt = (int64_t)slot * a.HV + h;
-        const int hk = h / a.group;
-        const float c = expf(__ldg(a.g + (int64_t)b * a.HV + h)) * __ldg(a.pool_gs + pt);
-        m.pt = pt;
-        m.b = b;
-        m.h = h;
-        m.drop = (c >= 0.0f && c < kDropBelow) ? 1 : 0;
-        m.c = m.drop ? 1.0f : c;
-        m.inv_c = 1.0f / m.c;
-        m.beta = __ldg(a.beta + (int64_t)b * a.HV + h);
-        m.end = 0;
-        uint64_t* bar = &sm.full[s];
-        mbar_arrive_expect_tx(bar, kStageTx);  // also publishes the metadata
-        asm volatile(
-            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-            "[%4];" ::"r"(smem_u32(st.codes)),
-            "l"(&tm_codes), "r"(0), "r"((int32_t)(pt * kD)), "r"(smem_u32(bar))
-            : "memory");
-        bulk_g2s(st.scales, a.pool_scales + pt * kScaleBytes, kScaleBytes, bar);
-        bulk_g2s(st.q, a.q + b * a.q_stride + (int64_t)hk * kD, kVecBytes, bar);
-        bulk_g2s(st.k, a.k + b * a.k_stride + (int64_t)hk * kD, kVecBytes, bar);
-        bulk_g2s(st.v, a.v + b * a.v_stride + (int64_t)h * kD, kVecBytes, bar);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        ++n;
+      }
+      cur = nxt;
+      tb0 += batch_step;
+    }
+    // walk over: an end marker in the ring
+    if (ok && lane == 0) {
+      const int s = n % kStages;
+      if (n < kStages || wait_bar(&sm.empty[s], (uint32_t)(((n / kStages) - 1) & 1), abort_flag)) {
+        sm.ring[n % kRing].end = 1;
+        mbar_arrive(&sm.full[s]);
       }
     }
     __syncwarp();
+  } else if (warp == kStageWarp) {
+    // =================================== staging ===================================
+    for (int n = 0;; ++n) {
+      const int s = n % kStages;
+      if (!wait_bar(&sm.full[s], (uint32_t)((n / kStages) & 1), abort_flag)) break;
+      TileMeta& m = sm.ring[n % kRing];
+      Stage& st = sm.st[s];
+      if (!m.end) {
+        uint32_t* sfw = reinterpret_cast<uint32_t*>(st.sfp);
+        const uint32_t* scw = reinterpret_cast<const uint32_t*>(st.scales);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const int qd = lane + 32 * r;
+          const int t = qd >> 7, m0 = (qd & 127) >> 2, m1 = qd & 3;
+          sfw[t * 128 + m0 * 4 + m1] = scw[(32 * m1 + m0) * 2 + t];
+        }
+        float kq = 0.0f;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int i2 = lane + 32 * r;  // pair (2 i2, 2 i2 + 1)
+          const __nv_bfloat162 k2 = reinterpret_cast<const __nv_bfloat162*>(st.k)[i2];
+          const __nv_bfloat162 q2 = reinterpret_cast<const __nv_bfloat162*>(st.q)[i2];
+          const float4 f = make_float4(__low2float(k2), __high2float(k2), __low2float(q2), __high2float(q2));
+          st.kq4[i2] = f;
+          kq = fmaf(f.x, f.z, fmaf(f.y, f.w, kq));
+          *reinterpret_cast<float2*>(st.ak + kf32(2 * i2, 0, 256)) = make_float2(f.x, f.x);
+          *reinterpret_cast<float2*>(st.ak + kf32(2 * i2 + 1, 0, 256)) = make_float2(f.y, f.y);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) kq += __shfl_xor_sync(0xffffffffu, kq, o);
+        if (lane == 0) m.kq = kq;
+        tc::fence_smem_to_async();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.ready[s]);  // publishes sfp, kq4, ak and m.kq
+      if (m.end) break;
+    }
   } else if (warp == kMmaWarp) {
     // ===================================== MMA =====================================
     const uint32_t id_mx = tc::idesc_mxf4nvf4(128, 128);
@@ -270,49 +351,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0)
       for (int kt = 0; kt < 2; ++kt) tc::cp_32x128b_warpx4(T + kColOne + 4 * kt, tc::smem_desc(sm.sf_one + 512 * kt, 0, 128));
     bool ok = true;
-    // Tile n's operands (after its stage landed): scale factors, k/q for the w
-    // warps, then MMA1' into D1'[n & 1].  Returns false at the end marker.
+    // Tile n: scale factors to TMEM and MMA1' into D1' (free: the w warps
+    // loaded tile n - 1's).
     auto front = [&](int n, bool& more) -> bool {
       const int s = n % kStages;
-      if (!wait_bar(&sm.full[s], (uint32_t)((n / kStages) & 1), abort_flag)) return false;
-      Stage& st = sm.st[s];
-      more = !st.meta.end;
+      if (!wait_bar(&sm.ready[s], (uint32_t)((n / kStages) & 1), abort_flag)) return false;
+      more = !sm.ring[n % kRing].end;
       if (!more) return true;
-      uint32_t* sfw = reinterpret_cast<uint32_t*>(sm.sfb[n & 1]);
-      const uint32_t* scw = reinterpret_cast<const uint32_t*>(st.scales);
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const int qd = lane + 32 * r;
-        const int t = qd >> 7, m0 = (qd & 127) >> 2, m1 = qd & 3;
-        sfw[t * 128 + m0 * 4 + m1] = scw[(32 * m1 + m0) * 2 + t];
-      }
-      float kq = 0.0f;
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int i2 = lane + 32 * r;  // pair (2 i2, 2 i2 + 1)
-        const __nv_bfloat162 k2 = reinterpret_cast<const __nv_bfloat162*>(st.k)[i2];
-        const __nv_bfloat162 q2 = reinterpret_cast<const __nv_bfloat162*>(st.q)[i2];
-        const float4 f = make_float4(__low2float(k2), __high2float(k2), __low2float(q2), __high2float(q2));
-        sm.kq4[n & 1][i2] = f;
-        kq = fmaf(f.x, f.z, fmaf(f.y, f.w, kq));
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) kq += __shfl_xor_sync(0xffffffffu, kq, o);
-      // D1'[n & 1] was last read by the w warps for tile n - 2 (bar_w waited since)
-      tc::fence_smem_to_async();
-      __syncwarp();
+      if (n >= 1 && !wait_bar(&sm.bar_tfree, (uint32_t)((n - 1) & 1), abort_flag)) return false;
+      tc::fence_after_sync();
       if (lane == 0) {
-        InfoW& iw = sm.iw[n & 1];
-        iw.m = st.meta;
-        iw.kq = kq;
-        iw.stage = s;
+        Stage& st = sm.st[s];
         const uint32_t sf = T + kColSF + 8 * (n % 3);
-        for (int kt = 0; kt < 2; ++kt) tc::cp_32x128b_warpx4(sf + 4 * kt, tc::smem_desc(sm.sfb[n & 1] + 512 * kt, 0, 128));
+        for (int kt = 0; kt < 2; ++kt) tc::cp_32x128b_warpx4(sf + 4 * kt, tc::smem_desc(st.sfp + 512 * kt, 0, 128));
         for (int kt = 0; kt < 2; ++kt)
-          tc::mma_mxf4nvf4(T + kColD1t + 128 * (n & 1), tc::smem_desc(sm.ident + 4096 * kt, 2048, 128),
-                           desc_codes(st.codes, kt), id_mx, T + kColOne + 4 * kt, sf + 4 * kt, kt > 0);
-        mbar_arrive(&sm.bar_t[n & 1]);  // publishes iw, kq4
-        tc::commit(&sm.bar_t[n & 1]);
+          tc::mma_mxf4nvf4(T + kColD1t, tc::smem_desc(sm.ident + 4096 * kt, 2048, 128), desc_codes(st.codes, kt),
+                           id_mx, T + kColOne + 4 * kt, sf + 4 * kt, kt > 0);
+        mbar_arrive(&sm.bar_t);  // publishes the ring entry to the w warps
+        tc::commit(&sm.bar_t);
       }
       __syncwarp();
       return true;
@@ -322,55 +378,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     int n = 0;
     for (; ok && more; ++n) {
       const int s = n % kStages;
-      Stage& st = sm.st[s];
-      // tile n + 1's decode goes ahead of tile n's update (D1'[(n + 1) & 1] is
-      // free: the w warps finished tile n - 1, waited for in the last iteration)
       bool more_next = false;
       if (!front(n + 1, more_next)) { ok = false; break; }
-      // MMA1(n) + MMA_r1(n) into D1 once w(n) is ready and the requantisers read D1 (tile n - 1)
-      if (!wait_bar(&sm.bar_w, (uint32_t)(n & 1), abort_flag)) { ok = false; break; }
-      if (n >= 1 && !wait_bar(&sm.bar_q, (uint32_t)((n - 1) & 1), abort_flag)) { ok = false; break; }
+      // MMA1(n) + MMA_r1(n) into D1[n & 1] once w(n) is ready and that group released tile n - 2
+      if (!wait_bar(&sm.bar_w[n & 1], (uint32_t)((n >> 1) & 1), abort_flag)) { ok = false; break; }
+      if (n >= 2 && !wait_bar(&sm.bar_q[n & 1], (uint32_t)(((n - 2) >> 1) & 1), abort_flag)) { ok = false; break; }
       tc::fence_after_sync();
-      uint8_t* ak = sm.ak[n & 1];
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int i = lane + 32 * r;
-        const float kv = bf2f(st.k[i]);
-        *reinterpret_cast<float*>(ak + kf32(i, 0, 256)) = kv;
-        *reinterpret_cast<float*>(ak + kf32(i, 1, 256)) = kv;
-      }
-      tc::fence_smem_to_async();
-      __syncwarp();
       if (lane == 0) {
-        sm.iq = st.meta;
+        Stage& st = sm.st[s];
+        const int drop = sm.ring[n % kRing].drop;
         const uint32_t sf = T + kColSF + 8 * (n % 3);
-        if (!st.meta.drop)
+        const uint32_t d = T + kColD1 + 128 * (n & 1);
+        if (!drop)
           for (int kt = 0; kt < 2; ++kt)
-            tc::mma_mxf4nvf4(T + kColD1, desc_codes(st.codes, kt), tc::smem_desc(sm.ident + 4096 * kt, 2048, 128),
-                             id_mx, sf + 4 * kt, T + kColOne + 4 * kt, kt > 0);
-        tc::mma_tf32_ss(T + kColD1, tc::smem_desc(ak, 128, 256), tc::smem_desc(sm.bw[n & 1], 128, 256), id_r1,
-                        st.meta.drop ? 0u : 1u);
-        mbar_arrive(&sm.bar_d);  // publishes iq
-        tc::commit(&sm.bar_d);
+            tc::mma_mxf4nvf4(d, desc_codes(st.codes, kt), tc::smem_desc(sm.ident + 4096 * kt, 2048, 128), id_mx,
+                             sf + 4 * kt, T + kColOne + 4 * kt, kt > 0);
+        tc::mma_tf32_ss(d, tc::smem_desc(st.ak, 128, 256), tc::smem_desc(sm.bw[n & 1], 128, 256), id_r1,
+                        drop ? 0u : 1u);
+        mbar_arrive(&sm.bar_d[n & 1]);  // publishes the ring entry to the requantisers
+        tc::commit(&sm.bar_d[n & 1]);
         tc::commit(&sm.empty[s]);
       }
       __syncwarp();
       more = more_next;
     }
-    // end: tell the w and requantiser warps (n = number of tiles)
+    // end: release the w warps and both requantiser groups into end markers
     if (ok) {
       const int N = n;
-      // w warps: an end marker in iw[N & 1] (they finished tile N - 2: bar_w(N - 1) seen)
-      if (lane == 0) {
-        sm.iw[N & 1].m.end = 1;
-        mbar_arrive(&sm.bar_t[N & 1]);
-        mbar_arrive(&sm.bar_t[N & 1]);
+      if (lane == 0) {  // the w warps read ring[N] (the producer's end marker)
+        mbar_arrive(&sm.bar_t);
+        mbar_arrive(&sm.bar_t);
       }
-      if (N >= 1) ok = wait_bar(&sm.bar_q, (uint32_t)((N - 1) & 1), abort_flag);
-      if (ok && lane == 0) {
-        sm.iq.end = 1;
-        mbar_arrive(&sm.bar_d);
-        mbar_arrive(&sm.bar_d);
+      for (int e = N; ok && e < N + 2; ++e) {  // group e & 1 reads ring[e]
+        if (e >= 2) ok = wait_bar(&sm.bar_q[e & 1], (uint32_t)(((e - 2) >> 1) & 1), abort_flag);
+        if (ok && lane == 0) {
+          sm.ring[e % kRing].end = 1;
+          mbar_arrive(&sm.bar_d[e & 1]);
+          mbar_arrive(&sm.bar_d[e & 1]);
+        }
       }
     }
     if (!ok) *abort_flag = 1;
@@ -382,35 +427,48 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp >= kWWarp0) {
     // ================================ w and outputs ================================
-    const int j = 32 * (warp & 3) + lane;
-    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    const int quad = warp & 3, half = (warp >> 2) & 1;
+    const int j = 32 * quad + lane;
+    const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
     for (int n = 0;; ++n) {
-      if (!wait_bar(&sm.bar_t[n & 1], (uint32_t)((n >> 1) & 1), abort_flag)) break;
-      const InfoW iw = sm.iw[n & 1];
-      if (iw.m.end) break;
+      // one thread waits; the others sleep on the group's hardware barrier
+      if (tid == 32 * kWWarp0) wait_bar(&sm.bar_t, (uint32_t)(n & 1), abort_flag);
+      named_bar(kBarW, 256);
+      if (*abort_flag) break;
+      const TileMeta m = sm.ring[n % kRing];
+      if (m.end) break;
+      const Stage& st = sm.st[n % kStages];
       tc::fence_after_sync();
-      // u / c, p / c = row j of D1' against k, q
+      // [u p] / c: this warp's half (64 columns i) of row j of D1', 32 at a time
       float2 su = make_float2(0.0f, 0.0f), sp = make_float2(0.0f, 0.0f);
-      const float4* kq4 = sm.kq4[n & 1];
+      const uint32_t ta = T + lane_base + kColD1t + 64 * half;
 #pragma unroll
-      for (int c32 = 0; c32 < 4; ++c32) {
+      for (int h2 = 0; h2 < 2; ++h2) {
         float2 x[16];
-        tc::ld_32x32b_x32(T + lane_base + kColD1t + 128 * (n & 1) + 32 * c32, reinterpret_cast<float*>(x));
+        tc::ld_32x32b_x32(ta + 32 * h2, reinterpret_cast<float*>(x));
         tc::ld_wait();
+        if (h2 == 1) {
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.bar_tfree);  // D1' is read
+        }
+        const float4* kq4 = st.kq4 + 32 * half + 16 * h2;
 #pragma unroll
         for (int p = 0; p < 16; ++p) {
-          const float4 kq = kq4[16 * c32 + p];
+          const float4 kq = kq4[p];
           su = __ffma2_rn(x[p], make_float2(kq.x, kq.y), su);
           sp = __ffma2_rn(x[p], make_float2(kq.z, kq.w), sp);
         }
       }
-      tc::fence_before_sync();
-      const TileMeta& m = iw.m;
+      if (half) sm.red[j] = make_float2(su.x + su.y, sp.x + sp.y);
+      named_bar(kBarW, 256);
+      if (half) continue;
+      const float2 r = sm.red[j];
       const float c = m.drop ? 0.0f : m.c;
-      const float u = su.x + su.y, p = sp.x + sp.y;
-      const float vj = bf2f(sm.st[iw.stage].v[j]);
+      const float u = su.x + su.y + r.x, p = sp.x + sp.y + r.y;
+      const float vj = bf2f(st.v[j]);
       const float wj = m.beta * (vj - c * u);
-      const float o = a.q_scale * fmaf(iw.kq, wj, c * p);
+      const float o = a.q_scale * fmaf(m.kq, wj, c * p);
       const float o1 = __shfl_down_sync(0xffffffffu, o, 1);
       if ((j & 1) == 0)
         reinterpret_cast<uint32_t*>(a.out + ((int64_t)m.b * a.HV + m.h) * kD)[j >> 1] =
@@ -422,74 +480,72 @@ __global__ void __launch_bounds__(kThreads, 1)
       *reinterpret_cast<float*>(bw + kf32(j, 1, 256)) = wc - hi;
       tc::fence_smem_to_async();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.bar_w);
+      if (lane == 0) mbar_arrive(&sm.bar_w[n & 1]);
     }
   } else {
     // ================================ requantisation ================================
-    const int quad = warp & 3, half = warp >> 2;
-    const int row = 32 * quad + lane;  // TMEM lane = state row i
+    const int grp = warp >> 3;                    // tiles n with n & 1 == grp
+    const int quad = warp & 3, half = (warp >> 2) & 1;
+    const int row = 32 * quad + lane;             // TMEM lane = state row i
     const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
-    for (int n = 0;; ++n) {
-      if (!wait_bar(&sm.bar_d, (uint32_t)(n & 1), abort_flag)) break;
-      const TileMeta m = sm.iq;
+    const int bar_id = grp ? kBarQ1 : kBarQ0;
+    const int lead = 256 * grp;                   // the group's first thread
+    for (int l = 0;; ++l) {
+      const int n = 2 * l + grp;
+      // one thread waits; the others sleep on the group's hardware barrier
+      if (tid == lead) wait_bar(&sm.bar_d[grp], (uint32_t)(l & 1), abort_flag);
+      named_bar(bar_id, 256);
+      if (*abort_flag) break;
+      const TileMeta m = sm.ring[n % kRing];
       if (m.end) break;
       tc::fence_after_sync();
-      float2 x[32];
-      {
-        const uint32_t ta = T + lane_base + kColD1 + 64 * half;
-        tc::ld_32x32b_x32(ta, reinterpret_cast<float*>(x));
-        tc::ld_32x32b_x32(ta + 32, reinterpret_cast<float*>(x) + 32);
-        tc::ld_wait();
-      }
-      // D1 and iq are read: release them to the MMA warp
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.bar_q);
-      // block abs-max: three-input max, NaN-propagating (a NaN block takes the exact path)
+      const uint32_t ta = T + lane_base + kColD1 + 128 * grp + 64 * half;
+      // pass 1: block maxima of this thread's 64 values
       float am[4];
       float tmax = 0.0f;
 #pragma unroll
-      for (int blk = 0; blk < 4; ++blk) {
-        const float2* xb = x + 8 * blk;
-        float m0, m1;
-        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(xb[0].x), "f"(xb[0].y), "f"(xb[1].x));
-        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m1) : "f"(xb[1].y), "f"(xb[2].x), "f"(xb[2].y));
-        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(m0), "f"(xb[3].x), "f"(xb[3].y));
-        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m1) : "f"(m1), "f"(xb[4].x), "f"(xb[4].y));
-        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(m0), "f"(xb[5].x), "f"(xb[5].y));
-        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m1) : "f"(m1), "f"(xb[6].x), "f"(xb[6].y));
-        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(m0), "f"(xb[7].x), "f"(xb[7].y));
-        float mb;
-        asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(mb) : "f"(m0), "f"(m1), "f"(0.0f));
-        am[blk] = mb;
-        float ok_max = mb;
-        if (isnan(mb)) {  // rare: the reference's amax ignores NaN
-          ok_max = 0.0f;
-#pragma unroll
-          for (int p = 0; p < 8; ++p) ok_max = fmaxf(ok_max, fmaxf(fabsf(xb[p].x), fabsf(xb[p].y)));
-        }
-        tmax = fmaxf(tmax, ok_max);
+      for (int h2 = 0; h2 < 2; ++h2) {
+        float2 x[16];
+        tc::ld_32x32b_x32(ta + 32 * h2, reinterpret_cast<float*>(x));
+        tc::ld_wait();
+        float a2[2];
+        tmax = fmaxf(tmax, block_amax3<2>(x, a2));
+        am[2 * h2] = a2[0];
+        am[2 * h2 + 1] = a2[1];
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
-      if (lane == 0) sm.amax[n & 1][warp] = tmax;
-      asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight requantiser warps
-      float amax = sm.amax[n & 1][0];
-#pragma unroll
-      for (int w = 1; w < kQWarps; ++w) amax = fmaxf(amax, sm.amax[n & 1][w]);
+      if (lane == 0) atomicMax(&sm.amax_bits[grp][l & 1], __float_as_uint(tmax));
+      named_bar(bar_id, 256);
+      const float amax = __uint_as_float(sm.amax_bits[grp][l & 1]);
+      // the next tile's slot: its last readers (tile n - 2) are past this barrier
+      if (tid == lead) sm.amax_bits[grp][(l + 1) & 1] = 0u;
       // S' = c D1: gs' = amax(S') / gden; y = D1 (c / gs')
       const float amax_s = m.c * amax;
       const float gs_new = (amax_s > 0.0f) ? __fdiv_rn(amax_s, a.gden) : 1.0f;
       const float mult = __fmul_rn(m.c, __frcp_rn(gs_new));
-      uint32_t words[8], scw;
-      requant_half_row<kMode>(
-          x, am, mult, sm.inv_tab, words, scw,
-          a.debug_y ? a.debug_y + (((int64_t)m.b * a.HV + m.h) * kD + row) * kD + 64 * half : nullptr);
-      uint4* dst = reinterpret_cast<uint4*>(a.pool_codes + m.pt * kCodeBytes + row * 64 + 32 * half);
-      dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
-      dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
+      // pass 2: quantise, one 16-value block at a time
+      uint8_t* codes = a.pool_codes + m.pt * kCodeBytes + row * 64 + 32 * half;
+      float* dbg = a.debug_y ? a.debug_y + (((int64_t)m.b * a.HV + m.h) * kD + row) * kD + 64 * half : nullptr;
+      uint32_t scw = 0;
+#pragma unroll
+      for (int blk = 0; blk < 4; ++blk) {
+        float2 x[8];
+        tc::ld_32x32b_x16(ta + 16 * blk, reinterpret_cast<float*>(x));
+        tc::ld_wait();
+        if (blk == 3) {  // D1 is read: release it to the MMA warp
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.bar_q[grp]);
+        }
+        const float a1[1] = {am[blk]};
+        uint32_t words[2], sc1;
+        requant_blocks<kMode, 1>(x, a1, mult, sm.inv_tab, words, sc1, dbg ? dbg + 16 * blk : nullptr);
+        *reinterpret_cast<uint2*>(codes + 8 * blk) = make_uint2(words[0], words[1]);
+        scw |= sc1 << (8 * blk);
+      }
       *reinterpret_cast<uint32_t*>(a.pool_scales + m.pt * kScaleBytes + row * 8 + 4 * half) = scw;
-      if (tid == 0) a.pool_gs[m.pt] = gs_new;
+      if (tid == lead) a.pool_gs[m.pt] = gs_new;
     }
   }
 

@@ -1,9 +1,9 @@
-// tile_requant.cuh -- requantisation of one 64-element half row of a 128 x 128
-// NVFP4 state tile, shared by the decode and prefill kernels.
+// tile_requant.cuh -- requantisation of whole 16-element scale blocks of a
+// 128 x 128 NVFP4 state tile, shared by the decode and prefill kernels.
 //
-// A CTA of 256 threads holds the tile as 128 rows x 2 halves; each thread owns
-// x[0..31] = 64 consecutive fp32 elements (pairs) of one row, i.e. four whole
-// 16-element scale blocks.  The tile's global scale is gs = amax / gden
+// Each thread owns whole 16-element scale blocks of one row (two or four,
+// i.e. a quarter or a half row) as fp32 pairs.  The tile's global scale is
+// gs = amax / gden
 // (1.0 for an all-zero tile) and every block goes through the reference block
 // quantiser (src/kernel/gdn_state_update_ref.cu:93-141) applied to
 // y = x * RN(1/gs): local scale amax_blk / 6, scale byte by the reference
@@ -38,19 +38,50 @@ __device__ __forceinline__ float block_amax4(const float2 (&x)[32], float (&am)[
   return tmax;
 }
 
-// Quantises the four blocks of x with the tile's inverse global scale.
-// am[blk] = max |x| of block blk as from block_amax4 (NaN when the block
-// holds one).  inv_tab[s] = 1 / decode(s) for every scale byte s.  Writes the
-// 32 code bytes (8 words, element order) and the four scale bytes (one word,
-// block order); debug_row, when set, receives the 64 fp32 quantiser inputs.
-template <int kMode>
-__device__ __forceinline__ void requant_half_row(const float2 (&x)[32], const float (&am)[4], float inv_gs,
-                                                 const float* inv_tab, uint32_t (&words)[8], uint32_t& scw,
-                                                 float* debug_row) {
+// Block max |x| with three-input max (sm_100): am[blk] = max |x| of block blk,
+// NaN when the block holds one (the requantiser then takes its exact path);
+// returns the NaN-ignoring maximum over the blocks.
+template <int NB>
+__device__ __forceinline__ float block_amax3(const float2 (&x)[8 * NB], float (&am)[NB]) {
+  float tmax = 0.0f;
+#pragma unroll
+  for (int blk = 0; blk < NB; ++blk) {
+    const float2* xb = x + 8 * blk;
+    float m0, m1, mb;
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(xb[0].x), "f"(xb[0].y), "f"(xb[1].x));
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m1) : "f"(xb[1].y), "f"(xb[2].x), "f"(xb[2].y));
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(m0), "f"(xb[3].x), "f"(xb[3].y));
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m1) : "f"(m1), "f"(xb[4].x), "f"(xb[4].y));
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(m0), "f"(xb[5].x), "f"(xb[5].y));
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m1) : "f"(m1), "f"(xb[6].x), "f"(xb[6].y));
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(m0), "f"(xb[7].x), "f"(xb[7].y));
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(mb) : "f"(m0), "f"(m1), "f"(0.0f));
+    am[blk] = mb;
+    float ok_max = mb;
+    if (isnan(mb)) {  // rare: the reference's amax ignores NaN
+      ok_max = 0.0f;
+#pragma unroll
+      for (int p = 0; p < 8; ++p) ok_max = fmaxf(ok_max, fmaxf(fabsf(xb[p].x), fabsf(xb[p].y)));
+    }
+    tmax = fmaxf(tmax, ok_max);
+  }
+  return tmax;
+}
+
+// Quantises the NB 16-element blocks of x with the tile's inverse global
+// scale.  am[blk] = max |x| of block blk (NaN when the block holds one).
+// inv_tab[s] = 1 / decode(s) for every scale byte s.  Writes the 8 NB code
+// bytes (2 NB words, element order) and the NB scale bytes (low bytes of
+// scw, block order); debug_row, when set, receives the 16 NB fp32 quantiser
+// inputs.
+template <int kMode, int NB>
+__device__ __forceinline__ void requant_blocks(const float2 (&x)[8 * NB], const float (&am)[NB], float inv_gs,
+                                               const float* inv_tab, uint32_t (&words)[2 * NB], uint32_t& scw,
+                                               float* debug_row) {
   const float2 r2 = make_float2(inv_gs, inv_gs);
   scw = 0;
 #pragma unroll
-  for (int blk = 0; blk < 4; ++blk) {
+  for (int blk = 0; blk < NB; ++blk) {
     float2 y[8];
 #pragma unroll
     for (int p = 0; p < 8; ++p) y[p] = __fmul2_rn(x[8 * blk + p], r2);
@@ -78,6 +109,14 @@ __device__ __forceinline__ void requant_half_row(const float2 (&x)[32], const fl
       for (int p = 0; p < 4; ++p) dy[p] = make_float4(y[2 * p].x, y[2 * p].y, y[2 * p + 1].x, y[2 * p + 1].y);
     }
   }
+}
+
+// The 64-element form used by the prefill epilogue.
+template <int kMode>
+__device__ __forceinline__ void requant_half_row(const float2 (&x)[32], const float (&am)[4], float inv_gs,
+                                                 const float* inv_tab, uint32_t (&words)[8], uint32_t& scw,
+                                                 float* debug_row) {
+  requant_blocks<kMode, 4>(x, am, inv_gs, inv_tab, words, scw, debug_row);
 }
 
 }  // namespace gdn
