@@ -105,6 +105,7 @@ struct __align__(1024) DecodeSmem {
   float2 red[kD];               // partial [u p] / c of the second half of each row of D1'
   TileMeta ring[kRing];         // metadata of valid tile n at n % kRing
   uint32_t amax_bits[2][2];     // per group, per tile parity: tile max |D1| as float bits
+  float2 gsm[2];                // per group: (gs', c / gs') of its current tile
   float inv_tab[256];
   uint64_t full[kStages], ready[kStages], empty[kStages];
   uint64_t bar_t, bar_tfree, bar_w[2], bar_d[2], bar_q[2], bar_fin;
@@ -163,7 +164,7 @@ __device__ __forceinline__ uint16_t f2bf_bits(float f) {
   return *reinterpret_cast<const uint16_t*>(&b);
 }
 
-template <int kMode>
+template <int kMode, bool kDebug>
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_decode_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_codes) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -440,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Stage& st = sm.st[n % kStages];
       tc::fence_after_sync();
       // [u p] / c: this warp's half (64 columns i) of row j of D1', 32 at a time
-      float2 su = make_float2(0.0f, 0.0f), sp = make_float2(0.0f, 0.0f);
+      float2 su0 = make_float2(0.0f, 0.0f), sp0 = su0, su1 = su0, sp1 = su0;
       const uint32_t ta = T + lane_base + kColD1t + 64 * half;
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
@@ -454,12 +455,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const float4* kq4 = st.kq4 + 32 * half + 16 * h2;
 #pragma unroll
-        for (int p = 0; p < 16; ++p) {
-          const float4 kq = kq4[p];
-          su = __ffma2_rn(x[p], make_float2(kq.x, kq.y), su);
-          sp = __ffma2_rn(x[p], make_float2(kq.z, kq.w), sp);
+        for (int p = 0; p < 16; p += 2) {
+          const float4 ka = kq4[p], kb = kq4[p + 1];
+          su0 = __ffma2_rn(x[p], make_float2(ka.x, ka.y), su0);
+          sp0 = __ffma2_rn(x[p], make_float2(ka.z, ka.w), sp0);
+          su1 = __ffma2_rn(x[p + 1], make_float2(kb.x, kb.y), su1);
+          sp1 = __ffma2_rn(x[p + 1], make_float2(kb.z, kb.w), sp1);
         }
       }
+      const float2 su = __fadd2_rn(su0, su1), sp = __fadd2_rn(sp0, sp1);
       if (half) sm.red[j] = make_float2(su.x + su.y, sp.x + sp.y);
       named_bar(kBarW, 256);
       if (half) continue;
@@ -517,16 +521,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
       if (lane == 0) atomicMax(&sm.amax_bits[grp][l & 1], __float_as_uint(tmax));
       named_bar(bar_id, 256);
-      const float amax = __uint_as_float(sm.amax_bits[grp][l & 1]);
-      // the next tile's slot: its last readers (tile n - 2) are past this barrier
-      if (tid == lead) sm.amax_bits[grp][(l + 1) & 1] = 0u;
-      // S' = c D1: gs' = amax(S') / gden; y = D1 (c / gs')
-      const float amax_s = m.c * amax;
-      const float gs_new = (amax_s > 0.0f) ? __fdiv_rn(amax_s, a.gden) : 1.0f;
-      const float mult = __fmul_rn(m.c, __frcp_rn(gs_new));
+      // S' = c D1: gs' = amax(S') / gden; y = D1 (c / gs'), computed once per group
+      if (tid == lead) {
+        const float amax_s = m.c * __uint_as_float(sm.amax_bits[grp][l & 1]);
+        const float gs_new = (amax_s > 0.0f) ? __fdiv_rn(amax_s, a.gden) : 1.0f;
+        sm.gsm[grp] = make_float2(gs_new, __fmul_rn(m.c, __frcp_rn(gs_new)));
+        sm.amax_bits[grp][(l + 1) & 1] = 0u;  // the next tile's slot (its last readers are past the barrier above)
+      }
+      named_bar(bar_id, 256);
+      const float2 gsm = sm.gsm[grp];
+      const float gs_new = gsm.x, mult = gsm.y;
       // pass 2: quantise, one 16-value block at a time
       uint8_t* codes = a.pool_codes + m.pt * kCodeBytes + row * 64 + 32 * half;
-      float* dbg = a.debug_y ? a.debug_y + (((int64_t)m.b * a.HV + m.h) * kD + row) * kD + 64 * half : nullptr;
+      float* dbg = kDebug ? a.debug_y + (((int64_t)m.b * a.HV + m.h) * kD + row) * kD + 64 * half : nullptr;
       uint32_t scw = 0;
 #pragma unroll
       for (int blk = 0; blk < 4; ++blk) {
@@ -540,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const float a1[1] = {am[blk]};
         uint32_t words[2], sc1;
-        requant_blocks<kMode, 1>(x, a1, mult, sm.inv_tab, words, sc1, dbg ? dbg + 16 * blk : nullptr);
+        requant_blocks<kMode, 1>(x, a1, mult, sm.inv_tab, words, sc1, kDebug ? dbg + 16 * blk : nullptr);
         *reinterpret_cast<uint2*>(codes + 8 * blk) = make_uint2(words[0], words[1]);
         scw |= sc1 << (8 * blk);
       }
@@ -644,21 +651,20 @@ extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
   const int64_t max_ctas = sm_count();
   const int grid = (int)(a.ntiles < max_ctas ? a.ntiles : max_ctas);
   // Opt in to > 48 KB of dynamic shared memory once per device and kernel.
-  static bool attr_set[2][64] = {};
+  static bool attr_set[4][64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GDN_ERR_CUDA;
-  const int mi = p->scale_mode == kScaleRef240 ? 0 : 1;
+  const int mi = (p->scale_mode == kScaleRef240 ? 0 : 1) + (p->debug_y ? 2 : 0);
+  void (*kern)(const DecodeArgs, const CUtensorMap) =
+      mi == 0 ? gdn_decode_kernel<kScaleRef240, false>
+      : mi == 1 ? gdn_decode_kernel<kScaleFn448, false>
+      : mi == 2 ? gdn_decode_kernel<kScaleRef240, true>
+                : gdn_decode_kernel<kScaleFn448, true>;
   if (!attr_set[mi][dev]) {
-    const cudaError_t e = mi == 0 ? cudaFuncSetAttribute(gdn_decode_kernel<kScaleRef240>,
-                                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
-                                  : cudaFuncSetAttribute(gdn_decode_kernel<kScaleFn448>,
-                                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return GDN_ERR_CUDA;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return GDN_ERR_CUDA;
     attr_set[mi][dev] = true;
   }
-  if (mi == 0)
-    gdn_decode_kernel<kScaleRef240><<<grid, kThreads, smem, stream>>>(a, tm);
-  else
-    gdn_decode_kernel<kScaleFn448><<<grid, kThreads, smem, stream>>>(a, tm);
+  kern<<<grid, kThreads, smem, stream>>>(a, tm);
   return launch_status();
 }
