@@ -36,6 +36,7 @@ import json
 import math
 import os
 import pathlib
+import re
 import statistics
 import sys
 import threading
@@ -158,58 +159,79 @@ def _max_over_ranks(dist, x: float) -> float:
 
 # ---- CPU path ---------------------------------------------------------------------------------
 
-def cpu_decode_sample(seconds: float, threads: int | None = None) -> dict:
-    """Times the CPU decode step on a bounded sample of the workload: repeated
-    passes over `sample_seqs` sequences (all 32 heads each) until `seconds`."""
-    import numpy as np
-    from gdn_b200 import workloads
-    from oracle import bindings as ob
+class CpuDecode:
+    """The CPU decode step on a bounded sample of the workload: `sample_seqs`
+    sequences (all 32 heads each) of the batch-256 decode step, set up once so
+    that every timed pass runs on warm buffers."""
 
-    lib, kind = ob.cpu_baseline(prefer_reference=True)
-    # the reference host codec saturates scales at 240: pair it with gs = amax/(6*240)
-    mode, gden = (0, 6.0 * 240.0) if kind == "reference" else (SCALE_MODE, 6.0 * 448.0)
-    nthreads = threads or lib.cpu_max_threads()
     sample_seqs = 16
-    x = workloads.decode_steps(sample_seqs, 1, HK, HV, D, seed=0)
-    states = workloads.initial_states(sample_seqs, HV, D, seed=1).numpy()
-    codes, scales, gs, _ = ob.quantise_tiles(states.reshape(-1), D * D, mode, gden)
-    codes = codes.reshape(sample_seqs, HV, D, D // 2).copy()
-    scales = scales.reshape(sample_seqs, HV, D, D // 16).copy()
-    gs = gs.reshape(sample_seqs, HV).copy()
 
-    def bits(t):
-        return np.ascontiguousarray(t.contiguous().view(__import__("torch").int16).numpy().view(np.uint16))
+    def __init__(self, threads: int | None = None):
+        import numpy as np
+        from gdn_b200 import workloads
+        from oracle import bindings as ob
 
-    q, k, v = bits(x["q"][0]), bits(x["k"][0]), bits(x["v"][0])
-    g, be = np.ascontiguousarray(x["g"][0].numpy()), np.ascontiguousarray(x["beta"][0].numpy())
-    slot = np.arange(sample_seqs, dtype=np.int32)
-    o = np.zeros((sample_seqs, HV, D), np.uint16)
-    P = ob._ptr
+        self.lib, self.kind = ob.cpu_baseline(prefer_reference=True)
+        # the reference host codec saturates scales at 240: pair it with gs = amax/(6*240)
+        self.mode, self.gden = (0, 6.0 * 240.0) if self.kind == "reference" else (SCALE_MODE, 6.0 * 448.0)
+        self.threads = threads or self.lib.cpu_max_threads()
+        n = self.sample_seqs
+        x = workloads.decode_steps(n, 1, HK, HV, D, seed=0)
+        states = workloads.initial_states(n, HV, D, seed=1).numpy()
+        codes, scales, gs, _ = ob.quantise_tiles(states.reshape(-1), D * D, self.mode, self.gden)
+        self.codes = codes.reshape(n, HV, D, D // 2).copy()
+        self.scales = scales.reshape(n, HV, D, D // 16).copy()
+        self.gs = gs.reshape(n, HV).copy()
+
+        def bits(t):
+            return np.ascontiguousarray(t.contiguous().view(__import__("torch").int16).numpy().view(np.uint16))
+
+        self.q, self.k, self.v = bits(x["q"][0]), bits(x["k"][0]), bits(x["v"][0])
+        self.g, self.beta = np.ascontiguousarray(x["g"][0].numpy()), np.ascontiguousarray(x["beta"][0].numpy())
+        self.slot = np.arange(n, dtype=np.int32)
+        self.o = np.zeros((n, HV, D), np.uint16)
+        self._ptr = ob._ptr
+
+    def run_pass(self) -> None:
+        P, n = self._ptr, self.sample_seqs
+        self.lib.cpu_gdn_decode(n, HK, HV, D, P(self.q), P(self.k), P(self.v), P(self.g), P(self.beta), P(self.slot),
+                                P(self.codes), P(self.scales), P(self.gs), P(self.o), 1.0 / math.sqrt(D), self.mode,
+                                self.gden, 0, n * HV, self.threads)
+
+    def describe(self, passes: int, seconds: float) -> str:
+        if self.kind != "reference":
+            return f"{passes} passes x {self.sample_seqs} sequences x {HV} heads; oracle port of the CPU path"
+        return (f"{passes} passes x {self.sample_seqs} sequences x {HV} heads of the same decode step "
+                f"({seconds:.1f} s); reference NVFP4 host codec (oracle/_ref) around a C restatement of the "
+                f"GDN step")
+
+
+def cpu_decode_sample(seconds: float, threads: int | None = None) -> dict:
+    """Times repeated warm passes of the CPU decode sample until `seconds`."""
+    cpu = CpuDecode(threads)
+    cpu.run_pass()  # warm-up: first touch of the sample's buffers
     calls = 0
     t0 = time.perf_counter()
     while True:
-        lib.cpu_gdn_decode(sample_seqs, HK, HV, D, P(q), P(k), P(v), P(g), P(be), P(slot), P(codes), P(scales),
-                           P(gs), P(o), 1.0 / math.sqrt(D), mode, gden, 0, sample_seqs * HV, nthreads)
+        cpu.run_pass()
         calls += 1
         el = time.perf_counter() - t0
         if el >= seconds:
             break
-    return {"value": calls * sample_seqs / el, "unit": UNIT, "cores": nthreads, "kind": kind,
-            "sample": (f"{calls} passes x {sample_seqs} sequences x {HV} heads of the same decode step "
-                       f"({el:.1f} s); reference NVFP4 host codec (oracle/_ref) around a C restatement of the "
-                       f"GDN step" if kind == "reference" else "oracle port of the CPU path")}
+    return {"value": calls * cpu.sample_seqs / el, "unit": UNIT, "cores": cpu.threads, "kind": cpu.kind,
+            "sample": cpu.describe(calls, el)}
 
 
 # ---- GPU path ---------------------------------------------------------------------------------------
 
-def _traffic_from_profile() -> float | None:
-    p = ROOT / "profiles" / "gdn_decode_b256_traffic.json"
-    if p.exists():
-        try:
-            return float(json.loads(p.read_text())["dram_bytes_per_launch"])
-        except Exception:
-            return None
-    return None
+def _traffic_from_profile(summary: str) -> float | None:
+    """DRAM bytes (read + write) per launch, from the `dram_bytes_per_launch = N`
+    line of an ncu summary under profiles/ (null when there is none)."""
+    p = ROOT / "profiles" / summary
+    if not p.exists():
+        return None
+    m = re.search(r"^dram_bytes_per_launch = (\d+)", p.read_text(), re.M)
+    return float(m.group(1)) if m else None
 
 
 def run_ours(args, dist, rank, world, local) -> dict | None:
@@ -267,8 +289,9 @@ def run_ours(args, dist, rank, world, local) -> dict | None:
         raise RuntimeError("device status set during the timed region")
 
     # e2e: through the public API with pinned host buffers.  Every step copies
-    # its own inputs host -> device and its outputs device -> host; a copy
-    # stream moves step i+1's inputs while step i computes (double buffers).
+    # its own inputs host -> device and its outputs device -> host; one copy
+    # stream moves step i+1's inputs and another step i-1's outputs while step
+    # i computes (double buffers).
     host_in = []
     for i in range(N_POOLS):
         x = inputs[i]
@@ -281,9 +304,12 @@ def run_ours(args, dist, rank, world, local) -> dict | None:
     h2d = sum(t.numel() * t.element_size() for t in host_in[0].values()) + host_slot.numel() * 4
     d2h = host_out[0].numel() * 2
     e2e_steps = max(1, min(args.steps, 200))
-    copy_stream = torch.cuda.Stream(dev)
+    copy_stream = torch.cuda.Stream(dev)   # host -> device, one step ahead
+    back_stream = torch.cuda.Stream(dev)   # device -> host, behind the compute
     loaded = [torch.cuda.Event() for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
+    drained = [torch.cuda.Event() for _ in range(2)]
 
     def load(i):
         b = i % 2
@@ -297,16 +323,23 @@ def run_ours(args, dist, rank, world, local) -> dict | None:
     def e2e_run(n):
         for b in range(2):
             consumed[b].record(stream)
+            drained[b].record(stream)
         load(0)
         for i in range(n):
             b = i % 2
             if i + 1 < n:
                 load(i + 1)
             stream.wait_event(loaded[b])
+            stream.wait_event(drained[b])  # the output buffer's previous copy-out is done
             x = dev_in[b]
             ops.decode(x["q"], x["k"], x["v"], x["g"], x["beta"], dev_slot[b], pools[i % N_POOLS], out=dev_out[b])
             consumed[b].record(stream)
-            host_out[b].copy_(dev_out[b], non_blocking=True)
+            computed[b].record(stream)
+            with torch.cuda.stream(back_stream):
+                back_stream.wait_event(computed[b])
+                host_out[b].copy_(dev_out[b], non_blocking=True)
+                drained[b].record(back_stream)
+        stream.wait_stream(back_stream)
 
     e2e_run(3)
     torch.cuda.synchronize()
@@ -338,7 +371,7 @@ def run_ours(args, dist, rank, world, local) -> dict | None:
         "e2e": {"value": round(B * world * e2e_steps / (e2e_ms / 1e3), 1), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": _traffic_from_profile(),
+                     "frac": round(achieved / peak, 4), "traffic": _traffic_from_profile("gdn_decode_b256.md"),
                      "peak_source": peak_note, "kernel": "gdn_decode_kernel",
                      "mean_launch_us": round(mean_launch_ms * 1e3, 3)},
         "gpu_launches": args.steps,
@@ -462,7 +495,7 @@ def run_prefill(args, dist, rank, world, local) -> dict | None:
         "e2e": {"value": round(tokens / (e_ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": host_out.numel() * 2},
         "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": tpeak, "unit": "TFLOP/s",
-                     "frac": round(tf / tpeak, 4), "traffic": None, "kernel": "gdn_prefill_kernel",
+                     "frac": round(tf / tpeak, 4), "traffic": _traffic_from_profile("gdn_prefill_8x8192.md"), "kernel": "gdn_prefill_kernel",
                      "mean_launch_us": round(launch_ms * 1e3, 2),
                      "hbm": {"achieved": round(gbs, 1), "peak": hpeak, "frac": round(gbs / hpeak, 4)}},
         "gpu_launches": args.steps, "clocks": clocks})
@@ -585,19 +618,19 @@ def run_layers(args, dist, rank, world, local) -> dict | None:
 def run_reference(args, rank) -> dict | None:
     if rank != 0:
         return None
-    per_step = []
-    info = None
+    cpu = CpuDecode()
     for _ in range(args.warmup):
-        cpu_decode_sample(0.0)
+        cpu.run_pass()
+    # each step: one pass over the 16-sequence sample; value: tokens/s over the timed steps
+    t0 = time.perf_counter()
     for _ in range(args.steps):
-        info = cpu_decode_sample(0.0)
-        per_step.append(info["value"])
-    # value: tokens/s over the timed steps (each step one bounded pass)
-    value = statistics.mean(per_step)
-    cb = {"value": round(value, 2), "unit": UNIT, "cores": info["cores"], "kind": info["kind"],
-          "sample": "each step: one pass of 16 sequences x 32 heads of the decode step; " + info["sample"]}
+        cpu.run_pass()
+    el = time.perf_counter() - t0
+    value = args.steps * cpu.sample_seqs / el
+    cb = {"value": round(value, 2), "unit": UNIT, "cores": cpu.threads, "kind": cpu.kind,
+          "sample": "each step: one pass of the decode step over a 16-sequence sample; " + cpu.describe(args.steps, el)}
     return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(16 / value * 1e3, 3), "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32 math, nvfp4 state, bf16 io", "data": "synthetic",
             "config": _config(args.gpus), "impl": "reference", "cpu_baseline": cb,
             "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -7,10 +7,15 @@
 //   * Shared-memory matrix descriptor (64 bit): start address >> 4 in bits
 //     0-13, leading-dimension byte offset >> 4 in 16-29, stride-dimension byte
 //     offset >> 4 in 32-45, version 1 in bit 46, layout (swizzle) in 61-63.
-//     Only the no-swizzle "interleaved" K-major layout is used here: 8-row x
-//     16-byte core matrices, rows 16 B apart, SBO = byte distance between
-//     consecutive 8-row groups, LBO = byte distance between the two 16-byte
-//     K chunks one MMA consumes.
+//     Three layouts are used here:
+//       - no swizzle (0), K-major: 8-row x 16-byte core matrices, rows 16 B
+//         apart, SBO = byte distance between consecutive 8-row groups, LBO =
+//         byte distance between the two 16-byte K chunks one MMA consumes;
+//       - 128-byte swizzle (2), K-major or MN-major: the layout TMA writes
+//         with CU_TENSOR_MAP_SWIZZLE_128B, 8 rows of 128 B per 1024-byte
+//         atom, SBO = distance between 8-row atoms;
+//       - 64-byte swizzle (4), K-major: rows of 64 B, 512-byte atoms (the
+//         layout of CU_TENSOR_MAP_SWIZZLE_64B).
 //   * All MMAs are issued by one thread; completion is signalled through
 //     tcgen05.commit on an mbarrier.
 #pragma once
