@@ -105,7 +105,6 @@ struct __align__(1024) DecodeSmem {
   float2 red[kD];               // partial [u p] / c of the second half of each row of D1'
   TileMeta ring[kRing];         // metadata of valid tile n at n % kRing
   uint32_t amax_bits[2][2];     // per group, per tile parity: tile max |D1| as float bits
-  float2 gsm[2];                // per group: (gs', c / gs') of its current tile
   float inv_tab[256];
   uint64_t full[kStages], ready[kStages], empty[kStages];
   uint64_t bar_t, bar_tfree, bar_w[2], bar_d[2], bar_q[2], bar_fin;
@@ -521,16 +520,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
       if (lane == 0) atomicMax(&sm.amax_bits[grp][l & 1], __float_as_uint(tmax));
       named_bar(bar_id, 256);
-      // S' = c D1: gs' = amax(S') / gden; y = D1 (c / gs'), computed once per group
-      if (tid == lead) {
-        const float amax_s = m.c * __uint_as_float(sm.amax_bits[grp][l & 1]);
-        const float gs_new = (amax_s > 0.0f) ? __fdiv_rn(amax_s, a.gden) : 1.0f;
-        sm.gsm[grp] = make_float2(gs_new, __fmul_rn(m.c, __frcp_rn(gs_new)));
-        sm.amax_bits[grp][(l + 1) & 1] = 0u;  // the next tile's slot (its last readers are past the barrier above)
-      }
-      named_bar(bar_id, 256);
-      const float2 gsm = sm.gsm[grp];
-      const float gs_new = gsm.x, mult = gsm.y;
+      // S' = c D1: gs' = amax(S') / gden; y = D1 (c / gs'), computed by every thread (no second barrier)
+      const float amax_s = m.c * __uint_as_float(sm.amax_bits[grp][l & 1]);
+      const float gs_new = (amax_s > 0.0f) ? __fdiv_rn(amax_s, a.gden) : 1.0f;
+      const float mult = __fmul_rn(m.c, __frcp_rn(gs_new));
+      if (tid == lead) sm.amax_bits[grp][(l + 1) & 1] = 0u;  // the next tile's slot: every thread of the
+                                                             // group read it (tile l - 1) before the barrier above
       // pass 2: quantise, one 16-value block at a time
       uint8_t* codes = a.pool_codes + m.pt * kCodeBytes + row * 64 + 32 * half;
       float* dbg = kDebug ? a.debug_y + (((int64_t)m.b * a.HV + m.h) * kD + row) * kD + 64 * half : nullptr;
