@@ -22,7 +22,7 @@
 // in shared memory is the operand of the two products that read the state.
 // Per chunk, all on tcgen05 except the 64 x 64 triangular solve:
 //   P1  (bf16)  [K; Q] K^T            -> K K^T and Q K^T in one M = 128 MMA
-//   Y   (bf16)  S^T K^T,  O1 (bf16) S^T Q^T          (with P1: they need only S)
+//   Y | O1      S^T [K; Q]^T in one N = 128 product   (with P1: they need only S)
 //   SIMT        A, P, T = (I + A)^-1 in 16 x 16 blocks
 //   P2  (bf16)  U^T = V^T (T diag beta)^T
 //   P4  (tf32)  U^T += Y (-T diag(beta gamma))^T     -> V_new^T
@@ -65,17 +65,19 @@ constexpr uint32_t kStage = 6 * kBox;
 constexpr uint32_t kOffStage = 0;                    // 2 stages
 constexpr uint32_t kOffSB = 2 * kStage;              // bf16 state copy S^T [j][i]
 constexpr uint32_t kOffScr = kOffSB + 32768;         // solve scratch -> V_new^T operands -> output staging
-constexpr uint32_t kSizeScr = 39168;
+constexpr uint32_t kSizeScr = 44032;
 constexpr uint32_t kOffTpp = kOffScr + kSizeScr;     // T diag(beta), bf16 [r][s]
 constexpr uint32_t kOffNtp = kOffTpp + 8192;         // -T diag(beta gamma), fp32 [r][s]
 constexpr uint32_t kOffPm = kOffNtp + 16384;         // P, bf16 [r][s]
 constexpr uint32_t kOffMisc = kOffPm + 8192;
 constexpr int kLd = 68;                              // solve scratch row pitch (floats)
+constexpr int kXLd = 16;                             // X^T row pitch (floats)
+constexpr int kDLd = 20;                             // diagonal-block inverse row pitch (floats)
 constexpr uint32_t kOPitch = 272;                    // output staging row pitch (bytes)
 constexpr uint32_t kFPitch = 132;                    // final-state transpose row pitch (floats)
 
 static_assert(kOffSB % 1024 == 0 && kStage % 1024 == 0, "swizzled stages need 1024-byte alignment");
-static_assert(2 * 64 * kLd * 4 + 16 * kLd * 4 <= kSizeScr, "solve scratch");
+static_assert(2 * 64 * kLd * 4 + 64 * kXLd * 4 + 64 * kDLd * 4 <= kSizeScr, "solve scratch");
 static_assert(2 * 16384 <= kSizeScr && 64 * kOPitch <= kSizeScr, "V_new operands / output staging");
 static_assert(kOffSB + 128 * kFPitch * 4 <= kOffTpp, "final-state transpose fits SB + scratch");
 static_assert(2 * kCodeBytes + 2 * kScaleBytes <= kSizeScr, "initial-state operands");
@@ -84,9 +86,9 @@ static_assert(2 * kCodeBytes + 2 * kScaleBytes <= kSizeScr, "initial-state opera
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;     // 128: state S^T (lane j, column i), fp32
 constexpr uint32_t kColKQ = 128;  // 64: [K K^T; Q K^T]
-constexpr uint32_t kColY = 192;   // 64: Y = S^T K^T
-constexpr uint32_t kColU = 256;   // 64: U^T, then V_new^T
-constexpr uint32_t kColO1 = 320;  // 64: S^T Q^T
+constexpr uint32_t kColY = 192;   // 64: Y = S^T K^T   } one N = 128 product
+constexpr uint32_t kColO1 = 256;  // 64: S^T Q^T       } S^T [K; Q]^T
+constexpr uint32_t kColU = 320;   // 64: U^T, then V_new^T
 constexpr uint32_t kColO2 = 384;  // 64: V_new^T P^T
 constexpr uint32_t kColSF = 448;  // 8: initial-state scale factors
 constexpr uint32_t kColOne = 456; // 8: unit scale factors
@@ -98,6 +100,7 @@ struct Misc {
   float bg[kC];    // beta * gamma
   float de[kC];    // exp(G_last - G)
   float qg[kC];    // q_scale * gamma
+  float al[kC];    // exp(g): one token's decay
   float inv_tab[256];
   float amax[kWarps];
   uint64_t bar_stg[2], bar_mma;
@@ -227,8 +230,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   uint8_t* const sb = smem + kOffSB;
   float* const Am = reinterpret_cast<float*>(smem + kOffScr);
-  float* const Tm = Am + 64 * kLd;
-  float* const Xm = Tm + 64 * kLd;
+  float* const Tt = Am + 64 * kLd;   // T^T: Tt[j * kLd + r] = T[r][j]
+  float* const Xt = Tt + 64 * kLd;   // X^T of the current block row: Xt[j * kXLd + t]
+  float* const Dm = Xt + 64 * kXLd;  // the diagonal blocks of T, row-major: Dm[(16 b + r) * kDLd + c]
   uint8_t* const vn = smem + kOffScr;           // V_new^T bf16 [j][s]
   uint8_t* const vnp = smem + kOffScr + 16384;  // V_new^T diag(exp(G_last - G)) bf16 [j][s]
   uint8_t* const ost = smem + kOffScr;          // output rows bf16 [r][j]
@@ -249,6 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_after_sync();
   const uint32_t T = ms.tmem_base;
   const uint32_t id_kq = tc::idesc_bf16(128, 64);
+  const uint32_t id_yo = tc::idesc_bf16(128, 128);
   const uint32_t id_u = tc::idesc_bf16(128, 64, true, false);
   const uint32_t id_s = tc::idesc_bf16(128, 128, false, true);
   const uint32_t id_tf = tc::idesc_tf32(128, 64);
@@ -384,8 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint64_t ds = tc::smem_desc(sb + 256 * ks, 128, 2048);
-          tc::mma_bf16_ss(T + kColY, ds, stage_kmajor(stage, kStK0, ks), id_kq, ks > 0);
-          tc::mma_bf16_ss(T + kColO1, ds, stage_kmajor(stage, kStQ0, ks), id_kq, ks > 0);
+          tc::mma_bf16_ss(T + kColY, ds, stage_kmajor(stage, kStK0, ks), id_yo, ks > 0);  // [Y | O1]
         }
       }
       tc::commit(&ms.bar_mma);
@@ -414,50 +418,53 @@ __global__ void __launch_bounds__(kThreads, 1)
       ms.bg[tid] = bv * gm;
       ms.de[tid] = __expf(Glast - G);
       ms.qg[tid] = a.q_scale * gm;
+      ms.al[tid] = __expf(gv);
     }
     if (!mma_wait()) { failed = true; break; }  // also publishes G, bet, bg, de, qg
 
     // ---- 1: A (strictly lower, for the solve) and P (lower incl. diagonal) ----
+    // The decay exp(G_r - G_s) of this thread's columns s in [sb0, sb0 + 32)
+    // comes from one exp at the last column s_hi <= r and a running product of
+    // per-token decays towards smaller s (exp(G_r - G_{s-1}) = exp(G_r - G_s)
+    // exp(g_s)): one exp per thread instead of one per element.
     {
       float vals[32];
       tc::ld_32x32b_x32(T + lane_base + kColKQ + 32 * half, vals);
       tc::ld_wait();
       const int sb0 = 32 * half;
-      if (quad < 2) {
-        const int r = lrow;
-        const float Gr = ms.G[r], br = ms.bet[r];
+      const bool arow = quad < 2;                  // rows 0-63: K K^T -> A; rows 64-127: Q K^T -> P
+      const int r = arow ? lrow : lrow - 64;
+      const int s_hi = arow ? r - 1 : r;           // last column kept
+      const float Gr = ms.G[r];
+      const float scale = arow ? ms.bet[r] : a.q_scale;
+      const int s_top = s_hi < sb0 + 31 ? s_hi : sb0 + 31;
+      float f = (s_top >= sb0) ? __expf(Gr - ms.G[s_top]) : 0.0f;
+      float o[32];
 #pragma unroll
-        for (int c4 = 0; c4 < 8; ++c4) {
-          const float4 Gs = *reinterpret_cast<const float4*>(ms.G + sb0 + 4 * c4);
-          const float gsv[4] = {Gs.x, Gs.y, Gs.z, Gs.w};
-          float o[4];
+      for (int e = 31; e >= 0; --e) {
+        const int s = sb0 + e;
+        if (s < s_top) f *= ms.al[s + 1];
+        o[e] = (s <= s_top) ? scale * vals[e] * f : 0.0f;
+      }
+      if (arow) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int s = sb0 + 4 * c4 + e;
-            o[e] = (s < r) ? br * vals[4 * c4 + e] * __expf(Gr - gsv[e]) : 0.0f;
-          }
-          *reinterpret_cast<float4*>(Am + r * kLd + sb0 + 4 * c4) = make_float4(o[0], o[1], o[2], o[3]);
-        }
+        for (int c4 = 0; c4 < 8; ++c4)
+          *reinterpret_cast<float4*>(Am + r * kLd + sb0 + 4 * c4) =
+              make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
       } else {
-        const int r = lrow - 64;
-        const float Gr = ms.G[r];
 #pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
-          float o[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int s = sb0 + 8 * c8 + e;
-            o[e] = (s <= r) ? a.q_scale * vals[8 * c8 + e] * __expf(Gr - ms.G[s]) : 0.0f;
-          }
+        for (int c8 = 0; c8 < 4; ++c8)
           *reinterpret_cast<uint4*>(pm + kbf16(r, sb0 + 8 * c8, 1024)) =
-              make_uint4(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]), pack_bf16(o[4], o[5]), pack_bf16(o[6], o[7]));
-        }
+              make_uint4(pack_bf16(o[8 * c8], o[8 * c8 + 1]), pack_bf16(o[8 * c8 + 2], o[8 * c8 + 3]),
+                         pack_bf16(o[8 * c8 + 4], o[8 * c8 + 5]), pack_bf16(o[8 * c8 + 6], o[8 * c8 + 7]));
       }
     }
     tc::fence_before_sync();
     __syncthreads();
 
     // ---- 2: T = (I + A)^-1 in 16 x 16 blocks ----
+    // T is kept transposed (a column of T is a contiguous row of Tt) so that
+    // the block products read both operands with 16-byte loads.
     if (tid < 64) {
       // diagonal blocks by forward substitution, one column per thread
       const int b = tid >> 4, c = tid & 15;
@@ -477,53 +484,58 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
         x[r] = (r < c) ? 0.0f : (r == c ? 1.0f : -sum);
       }
+      float4* tcol = reinterpret_cast<float4*>(Tt + (16 * b + c) * kLd + 16 * b);
 #pragma unroll
-      for (int r = 0; r < 16; ++r) Tm[(16 * b + r) * kLd + 16 * b + c] = x[r];
+      for (int r4 = 0; r4 < 4; ++r4) tcol[r4] = make_float4(x[4 * r4], x[4 * r4 + 1], x[4 * r4 + 2], x[4 * r4 + 3]);
+#pragma unroll
+      for (int r = 0; r < 16; ++r) Dm[(16 * b + r) * kDLd + c] = x[r];
     } else {
-      // zero the blocks above the diagonal
+      // zero the blocks above the diagonal: T[i][j] = Tt[j][i] with block(i) < block(j)
       for (int e = tid - 64; e < 6 * 256; e += kThreads - 64) {
         const int blk = e >> 8, idx = e & 255;
         const int bi = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
         const int bj = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
-        Tm[(16 * bi + (idx >> 4)) * kLd + 16 * bj + (idx & 15)] = 0.0f;
+        Tt[(16 * bj + (idx >> 4)) * kLd + 16 * bi + (idx & 15)] = 0.0f;
       }
     }
     __syncthreads();
 #pragma unroll
     for (int ib = 1; ib < 4; ++ib) {
       const int r = tid & 15, jj = tid >> 4;
-      // X = A[block row ib][0 : 16 ib] T[0 : 16 ib][0 : 16 ib]
+      // X = A[block row ib][0 : 16 ib] T[0 : 16 ib][0 : 16 ib]  (column j of T is zero above row 16 m)
 #pragma unroll
       for (int m = 0; m < ib; ++m) {
         const int j = jj + 16 * m;
         const float4* arow = reinterpret_cast<const float4*>(Am + (16 * ib + r) * kLd);
+        const float4* tcol = reinterpret_cast<const float4*>(Tt + j * kLd);
         float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (int k4 = 4 * m; k4 < 4 * ib; ++k4) {
-          const float4 av = arow[k4];
-          acc[0] = fmaf(av.x, Tm[(4 * k4 + 0) * kLd + j], acc[0]);
-          acc[1] = fmaf(av.y, Tm[(4 * k4 + 1) * kLd + j], acc[1]);
-          acc[2] = fmaf(av.z, Tm[(4 * k4 + 2) * kLd + j], acc[2]);
-          acc[3] = fmaf(av.w, Tm[(4 * k4 + 3) * kLd + j], acc[3]);
+          const float4 av = arow[k4], tv = tcol[k4];
+          acc[0] = fmaf(av.x, tv.x, acc[0]);
+          acc[1] = fmaf(av.y, tv.y, acc[1]);
+          acc[2] = fmaf(av.z, tv.z, acc[2]);
+          acc[3] = fmaf(av.w, tv.w, acc[3]);
         }
-        Xm[r * kLd + j] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+        Xt[j * kXLd + r] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
       }
       __syncthreads();
       // T[block row ib][0 : 16 ib] = -D_ib X
 #pragma unroll
       for (int m = 0; m < ib; ++m) {
         const int j = jj + 16 * m;
-        const float4* drow = reinterpret_cast<const float4*>(Tm + (16 * ib + r) * kLd + 16 * ib);
+        const float4* drow = reinterpret_cast<const float4*>(Dm + (16 * ib + r) * kDLd);
+        const float4* xcol = reinterpret_cast<const float4*>(Xt + j * kXLd);
         float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (int t4 = 0; t4 < 4; ++t4) {
-          const float4 dv = drow[t4];
-          acc[0] = fmaf(dv.x, Xm[(4 * t4 + 0) * kLd + j], acc[0]);
-          acc[1] = fmaf(dv.y, Xm[(4 * t4 + 1) * kLd + j], acc[1]);
-          acc[2] = fmaf(dv.z, Xm[(4 * t4 + 2) * kLd + j], acc[2]);
-          acc[3] = fmaf(dv.w, Xm[(4 * t4 + 3) * kLd + j], acc[3]);
+          const float4 dv = drow[t4], xv = xcol[t4];
+          acc[0] = fmaf(dv.x, xv.x, acc[0]);
+          acc[1] = fmaf(dv.y, xv.y, acc[1]);
+          acc[2] = fmaf(dv.z, xv.z, acc[2]);
+          acc[3] = fmaf(dv.w, xv.w, acc[3]);
         }
-        Tm[(16 * ib + r) * kLd + j] = -((acc[0] + acc[1]) + (acc[2] + acc[3]));
+        Tt[j * kLd + 16 * ib + r] = -((acc[0] + acc[1]) + (acc[2] + acc[3]));
       }
       __syncthreads();
     }
@@ -531,9 +543,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int sp = 0; sp < 2; ++sp) {
       const int r = tid & 63, s8 = 2 * (tid >> 6) + sp;
-      const float4 t0v = *reinterpret_cast<const float4*>(Tm + r * kLd + 8 * s8);
-      const float4 t1v = *reinterpret_cast<const float4*>(Tm + r * kLd + 8 * s8 + 4);
-      const float tv[8] = {t0v.x, t0v.y, t0v.z, t0v.w, t1v.x, t1v.y, t1v.z, t1v.w};
+      float tv[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) tv[e] = Tt[(8 * s8 + e) * kLd + r];
       uint32_t pb[4];
       float nt[8];
 #pragma unroll
