@@ -174,7 +174,8 @@ class CpuDecode:
         self.lib, self.kind = ob.cpu_baseline(prefer_reference=True)
         # the reference host codec saturates scales at 240: pair it with gs = amax/(6*240)
         self.mode, self.gden = (0, 6.0 * 240.0) if self.kind == "reference" else (SCALE_MODE, 6.0 * 448.0)
-        self.threads = threads or self.lib.cpu_max_threads()
+        # every host core this process may run on (torchrun sets OMP_NUM_THREADS=1 per rank)
+        self.threads = threads or max(len(os.sched_getaffinity(0)), self.lib.cpu_max_threads())
         n = self.sample_seqs
         x = workloads.decode_steps(n, 1, HK, HV, D, seed=0)
         states = workloads.initial_states(n, HV, D, seed=1).numpy()

@@ -96,7 +96,7 @@ __device__ __forceinline__ bool mbar_wait_cta(uint64_t* bar, uint32_t parity, ui
 }
 
 // 1-D bulk copy global -> shared, completing `bytes` on the mbarrier.
-// dst, src 16-byte aligned, bytes a multiple of 16.  No multicast.
+// dst, src 16-byte aligned, bytes a multiple of 16; into this CTA only.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

@@ -439,11 +439,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float scale = arow ? ms.bet[r] : a.q_scale;
       const int s_top = s_hi < sb0 + 31 ? s_hi : sb0 + 31;
       float f = (s_top >= sb0) ? __expf(Gr - ms.G[s_top]) : 0.0f;
+      // exp(g) of tokens sb0 + 1 .. sb0 + 32, in registers before the chain
+      float alv[33];
+#pragma unroll
+      for (int c4 = 0; c4 < 8; ++c4) {
+        const float4 t = *reinterpret_cast<const float4*>(ms.al + sb0 + 4 * c4);
+        alv[4 * c4] = t.x;
+        alv[4 * c4 + 1] = t.y;
+        alv[4 * c4 + 2] = t.z;
+        alv[4 * c4 + 3] = t.w;
+      }
+      alv[32] = half ? 1.0f : ms.al[32];  // token 64 does not exist (never used: s < s_top <= 63)
       float o[32];
 #pragma unroll
       for (int e = 31; e >= 0; --e) {
         const int s = sb0 + e;
-        if (s < s_top) f *= ms.al[s + 1];
+        if (s < s_top) f *= alv[e + 1];
         o[e] = (s <= s_top) ? scale * vals[e] * f : 0.0f;
       }
       if (arow) {

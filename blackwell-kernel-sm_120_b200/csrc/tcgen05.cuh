@@ -220,7 +220,7 @@ __device__ __forceinline__ void st_32x32b_x32(uint32_t taddr, const float* v) {
 
 __device__ __forceinline__ void st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// ---- TMA tensor load (no multicast) -----------------------------------------------------------
+// ---- TMA tensor load (this CTA only) ------------------------------------------------------------
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int c0, int c1, int c2, uint64_t* bar) {
   asm volatile(
