@@ -17,24 +17,24 @@
 // per token and sequence, src/ops/qwen35_gdn_patch.py:98-116).
 //
 // One CTA owns one (sequence, value head) at a time and walks its chunks in
-// order.  The fp32 state stays in tensor memory for the whole sequence,
-// transposed (TMEM lane = j over d_v, column = i over d_k); a bf16 copy of it
-// in shared memory is the operand of the two products that read the state.
-// Per chunk, all on tcgen05 except the 64 x 64 triangular solve:
-//   P1  (bf16)  [K; Q] K^T            -> K K^T and Q K^T in one M = 128 MMA
-//   Y | O1      S^T [K; Q]^T in one N = 128 product   (with P1: they need only S)
-//   SIMT        A, P, T = (I + A)^-1 in 16 x 16 blocks
-//   P2  (bf16)  U^T = V^T (T diag beta)^T
-//   P4  (tf32)  U^T += Y (-T diag(beta gamma))^T     -> V_new^T
-//   P6  (bf16)  O2 = V_new^T P^T
-//   P7  (bf16)  S^T <- gamma_{C-1} S^T + (V_new^T diag(exp(G_{C-1} - G))) K
-// q, k, v arrive by TMA tensor copies (128-byte swizzle) into a double-
-// buffered stage that the MMAs read in place: K and Q as K-major operands,
-// V and K as MN-major ones; the next-but-one chunk is loaded as soon as a
-// stage is released.  Outputs are staged in shared memory and stored as
-// 16-byte rows.  At the end of a sequence the state is requantised into its
-// pool slot with the reference block quantiser (tile_requant.cuh).  Every
-// wait is bounded.
+// order, in two warp groups that overlap consecutive chunks:
+//   prep  (warps 0-7)   the state-independent half of chunk c + 1: P1 = [K; Q] K^T
+//                       on the tensor cores, the gates, A and P, the triangular
+//                       solve T = (I + A)^-1 (SIMT), T diag(beta) and
+//                       -T diag(beta gamma), and P2: U^T = V^T (T diag beta)^T;
+//   chain (warps 8-15)  the state chain of chunk c: Y | O1 = S^T [K; Q]^T,
+//                       P4: V_new^T = U^T + Y (-T diag(beta gamma))^T (tf32, Y
+//                       read from TMEM), V_new^T packed to bf16 in TMEM, the
+//                       state decay, P6: O2 = V_new^T P^T and P7: S^T +=
+//                       V_new'^T K (both with A in TMEM), the outputs and the
+//                       bf16 copy of S for the next chunk.
+// The fp32 state stays in tensor memory for the whole sequence, transposed
+// (TMEM lane = j over d_v, column = i over d_k).  k and q arrive by TMA
+// tensor copies (128-byte swizzle) into a two-stage ring, v into its own
+// buffer; the MMAs read them in place.  The groups hand over through
+// double-buffered shared memory and TMEM, ordered by mbarriers.  At the end
+// of a sequence the state is requantised into its pool slot with the
+// reference block quantiser (tile_requant.cuh).  Every wait is bounded.
 #include <cstdint>
 #include <mutex>
 #include <cuda.h>
@@ -51,63 +51,76 @@ namespace {
 
 constexpr int kD = 128;
 constexpr int kC = 64;
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
+constexpr int kThreads = 512;       // prep warps 0-7, chain warps 8-15
+constexpr int kGroup = 256;         // threads per group
+constexpr int kBarPrep = 1, kBarChain = 2;  // named hardware barriers of the groups
 constexpr uint32_t kCodeBytes = kD * kD / 2;
 constexpr uint32_t kScaleBytes = kD * kD / 16;
 
-// One stage: six 64-row x 128-byte TMA boxes, 128-byte swizzled.
+// 64-row x 128-byte TMA boxes, 128-byte swizzled.
 constexpr uint32_t kBox = 8192;
-constexpr uint32_t kStK0 = 0, kStQ0 = kBox, kStK1 = 2 * kBox, kStQ1 = 3 * kBox, kStV0 = 4 * kBox, kStV1 = 5 * kBox;
-constexpr uint32_t kStage = 6 * kBox;
+constexpr uint32_t kStK0 = 0, kStQ0 = kBox, kStK1 = 2 * kBox, kStQ1 = 3 * kBox;  // one k/q stage
+constexpr uint32_t kStageKQ = 4 * kBox;
+constexpr uint32_t kV0 = 0, kV1 = kBox;  // the v buffer
 
 // Shared-memory map (bytes).
-constexpr uint32_t kOffStage = 0;                    // 2 stages
-constexpr uint32_t kOffSB = 2 * kStage;              // bf16 state copy S^T [j][i]
-constexpr uint32_t kOffScr = kOffSB + 32768;         // solve scratch -> V_new^T operands -> output staging
-constexpr uint32_t kSizeScr = 44032;
-constexpr uint32_t kOffTpp = kOffScr + kSizeScr;     // T diag(beta), bf16 [r][s]
-constexpr uint32_t kOffNtp = kOffTpp + 8192;         // -T diag(beta gamma), fp32 [r][s]
-constexpr uint32_t kOffPm = kOffNtp + 16384;         // P, bf16 [r][s]
-constexpr uint32_t kOffMisc = kOffPm + 8192;
+constexpr uint32_t kOffKQ = 0;                       // 2 k/q stages
+constexpr uint32_t kOffV = 2 * kStageKQ;             // v of the chunk the prep group works on
+constexpr uint32_t kOffSB = kOffV + 2 * kBox;        // chain: bf16 state copy S^T [j][i]
+constexpr uint32_t kOffScr = kOffSB + 32768;         // prep: solve scratch, T diag(beta)
 constexpr int kLd = 68;                              // solve scratch row pitch (floats)
 constexpr int kXLd = 16;                             // X^T row pitch (floats)
 constexpr int kDLd = 20;                             // diagonal-block inverse row pitch (floats)
-constexpr uint32_t kOPitch = 272;                    // output staging row pitch (bytes)
+constexpr uint32_t kSizeScr = 2 * 64 * kLd * 4 + 64 * kXLd * 4 + 64 * kDLd * 4;
+constexpr uint32_t kOffHand = kOffScr + kSizeScr;    // prep -> chain, double-buffered
 constexpr uint32_t kFPitch = 132;                    // final-state transpose row pitch (floats)
 
-static_assert(kOffSB % 1024 == 0 && kStage % 1024 == 0, "swizzled stages need 1024-byte alignment");
-static_assert(2 * 64 * kLd * 4 + 64 * kXLd * 4 + 64 * kDLd * 4 <= kSizeScr, "solve scratch");
-static_assert(2 * 16384 <= kSizeScr && 64 * kOPitch <= kSizeScr, "V_new operands / output staging");
-static_assert(kOffSB + 128 * kFPitch * 4 <= kOffTpp, "final-state transpose fits SB + scratch");
-static_assert(2 * kCodeBytes + 2 * kScaleBytes <= kSizeScr, "initial-state operands");
-
-// TMEM columns (512 allocated: one CTA per SM)
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;     // 128: state S^T (lane j, column i), fp32
-constexpr uint32_t kColKQ = 128;  // 64: [K K^T; Q K^T]
-constexpr uint32_t kColY = 192;   // 64: Y = S^T K^T   } one N = 128 product
-constexpr uint32_t kColO1 = 256;  // 64: S^T Q^T       } S^T [K; Q]^T
-constexpr uint32_t kColU = 320;   // 64: U^T, then V_new^T
-constexpr uint32_t kColO2 = 384;  // 64: V_new^T P^T
-constexpr uint32_t kColSF = 448;  // 8: initial-state scale factors
-constexpr uint32_t kColOne = 456; // 8: unit scale factors
+// One prep -> chain hand-over.
+struct Hand {
+  uint8_t ntp[64 * 64 * 4];  // -T diag(beta gamma), fp32 K-major [r][s]: B of P4
+  uint8_t pm[64 * 64 * 2];   // P, bf16 K-major [r][s]: B of P6
+  float de[kC];              // exp(G_last - G_s)
+  float qg[kC];              // q_scale * gamma_r
+  float gC;                  // gamma_{C-1}: the state's decay over the chunk
+  float pad[63];
+};
+constexpr uint32_t kOffMisc = kOffHand + 2 * sizeof(Hand);
 
 struct Misc {
   float gw[kC];    // warp-inclusive scans of g
   float G[kC];     // cumulative log decay
   float bet[kC];   // beta
   float bg[kC];    // beta * gamma
-  float de[kC];    // exp(G_last - G)
-  float qg[kC];    // q_scale * gamma
   float al[kC];    // exp(g): one token's decay
   float inv_tab[256];
-  float amax[kWarps];
-  uint64_t bar_stg[2], bar_mma;
+  float amax[8];
+  uint64_t bar_kq[2];     // k/q stage loaded
+  uint64_t bar_v;         // v loaded
+  uint64_t bar_p1;        // prep: P1 done
+  uint64_t bar_p2[2];     // prep: hand-over written (arrive) and P2 done (commit)
+  uint64_t bar_hfree[2];  // chain: hand-over and U[b] read (P4, P6, P7 done)
+  uint64_t bar_cm;        // chain: its MMAs done
+  uint64_t bar_seq;       // chain: a sequence's final state written, the prep scratch is free
   uint32_t tmem_base;
 };
 constexpr uint32_t kSmemBytes = kOffMisc + sizeof(Misc);
+static_assert(kOffKQ % 1024 == 0 && kOffV % 1024 == 0 && kStageKQ % 1024 == 0, "swizzled boxes: 1024-byte aligned");
+static_assert(sizeof(Hand) % 16 == 0 && kOffHand % 16 == 0, "hand-over alignment");
 static_assert(kSmemBytes <= 232448, "shared memory");
+static_assert(128 * kFPitch * 4 <= 32768 + kSizeScr, "final-state transpose fits SB + scratch");
+static_assert(2 * kCodeBytes + 2 * kScaleBytes <= 32768, "initial-state operands fit SB");
+static_assert(64 * 64 * 2 <= 64 * kLd * 4, "T diag(beta) fits the A scratch");
+
+// TMEM columns (512 allocated: one CTA per SM)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0;     // 128: state S^T (lane j, column i), fp32
+constexpr uint32_t kColY = 128;   // 64: Y = S^T K^T   } one N = 128 product
+constexpr uint32_t kColO1 = 192;  // 64: S^T Q^T       } S^T [K; Q]^T
+constexpr uint32_t kColO2 = 256;  // 64: V_new^T P^T
+constexpr uint32_t kColSF = 256;  // 8: initial-state scale factors (sequence start only, over O2)
+constexpr uint32_t kColOne = 264; // 8: unit scale factors (likewise)
+constexpr uint32_t kColKQ = 320;  // 64: [K K^T; Q K^T] (prep)
+constexpr uint32_t kColU = 384;   // 2 x 64: U^T -> V_new^T (fp32) -> [V_new^T | V_new'^T] (bf16 pairs)
 
 struct PrefillArgs {
   int32_t N, HK, HV, group, nitems;
@@ -139,6 +152,27 @@ __device__ __forceinline__ int canon(int row, int byte) { return (byte & 15) + 1
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&p);
+}
+
+// Named barrier over one warp group.
+__device__ __forceinline__ void group_sync(int id) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "n"(kGroup) : "memory");
+}
+// Named barrier over one warp group that also ORs a predicate across it.
+__device__ __forceinline__ bool group_or(int id, bool p) {
+  uint32_t r;
+  asm volatile(
+      "{ .reg .pred pi, po; setp.ne.u32 pi, %1, 0; bar.red.or.pred po, %2, %3, pi; selp.u32 %0, 1, 0, po; }"
+      : "=r"(r)
+      : "r"((uint32_t)p), "r"(id), "n"(kGroup)
+      : "memory");
+  return r != 0;
+}
+// The group's leader waits (bounded); every thread of the group learns the outcome.
+__device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, bool leader, int id) {
+  bool ok = true;
+  if (leader) ok = mbar_wait_bounded(bar, parity);
+  return !group_or(id, !ok);
 }
 
 // Position in the CTA's work list: item = n * HV + h, chunk of that sequence.
@@ -180,20 +214,26 @@ __device__ __forceinline__ int chunk_len(const Cursor& c) {
   return rest < kC ? (int)rest : kC;
 }
 
-// Thread 0: queue chunk c's k, q, v boxes into a stage.  Rows past the end of
-// the tensors arrive as zeros; rows past the end of the sequence are masked
-// by the consumers.
-__device__ __forceinline__ void issue_chunk(const PrefillArgs& a, uint8_t* stage, uint64_t* bar, const Cursor& c,
-                                            const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv) {
+// One thread: queue chunk c's k and q boxes into a stage.  Rows past the end
+// of the tensors arrive as zeros; rows past the end of the sequence are
+// masked by the consumers (beta = 0, rows not stored).
+__device__ __forceinline__ void issue_kq(const PrefillArgs& a, uint8_t* stage, uint64_t* bar, const Cursor& c,
+                                         const CUtensorMap* tq, const CUtensorMap* tk) {
   const int t0 = (int)(c.bos + c.chunk * kC);
   const int hk = c.h / a.group;
-  mbar_arrive_expect_tx(bar, kStage);
+  mbar_arrive_expect_tx(bar, kStageKQ);
   tc::tma_load_3d(stage + kStK0, tk, 0, hk, t0, bar);
   tc::tma_load_3d(stage + kStK1, tk, 64, hk, t0, bar);
   tc::tma_load_3d(stage + kStQ0, tq, 0, hk, t0, bar);
   tc::tma_load_3d(stage + kStQ1, tq, 64, hk, t0, bar);
-  tc::tma_load_3d(stage + kStV0, tv, 0, c.h, t0, bar);
-  tc::tma_load_3d(stage + kStV1, tv, 64, c.h, t0, bar);
+}
+
+__device__ __forceinline__ void issue_v(const PrefillArgs& a, uint8_t* vbuf, uint64_t* bar, const Cursor& c,
+                                        const CUtensorMap* tv) {
+  const int t0 = (int)(c.bos + c.chunk * kC);
+  mbar_arrive_expect_tx(bar, 2 * kBox);
+  tc::tma_load_3d(vbuf + kV0, tv, 0, c.h, t0, bar);
+  tc::tma_load_3d(vbuf + kV1, tv, 64, c.h, t0, bar);
 }
 
 // Threads 0..63: g and beta of token `r` of chunk c (0 past the chunk end).
@@ -207,9 +247,21 @@ __device__ __forceinline__ void load_gb(const PrefillArgs& a, const Cursor& c, i
   }
 }
 
-// K-major descriptor of rows [8 g, 8 g + 64 or 128) of a stage's K or Q, K step ks (16 elements).
+// K-major descriptor of rows [0, 64 or 128) of a stage's K or [K; Q], K step ks (16 elements).
 __device__ __forceinline__ uint64_t stage_kmajor(const uint8_t* stage, uint32_t box0, int ks) {
   return tc::smem_desc_sw128(stage + box0 + (ks < 4 ? 0u : 2u * kBox) + 32u * (ks & 3), 16, 1024);
+}
+
+// The slot of a sequence (-1: none or out of range) and whether it starts from the pool state.
+__device__ __forceinline__ int32_t seq_slot(const PrefillArgs& a, int n, bool report, bool& has) {
+  int32_t slot = a.slot_idx ? __ldg(a.slot_idx + n) : -1;
+  if (slot >= a.num_slots) {
+    if (report) atomicOr(a.status, GDN_STATUS_BAD_SLOT);
+    slot = -1;
+  }
+  if (slot < 0) slot = -1;
+  has = slot >= 0 && a.has_init && __ldg(a.has_init + n) != 0;
+  return slot;
 }
 
 template <int kMode>
@@ -219,32 +271,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem[];
   Misc& ms = *reinterpret_cast<Misc*>(smem + kOffMisc);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quad = warp & 3, half = warp >> 2;
+  const int quad = warp & 3, half = (warp >> 2) & 1;
   const int lrow = 32 * quad + lane;  // this thread's TMEM lane
   const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
 
-  // The swizzled stages need a 1024-byte aligned window.
+  // The swizzled boxes need a 1024-byte aligned window.
   if ((smem_u32(smem) & 1023u) != 0) {
     if (tid == 0) atomicOr(a.status, kStatusWaitTimeout);
     return;
   }
+  Hand* const hand = reinterpret_cast<Hand*>(smem + kOffHand);
+  uint8_t* const vbuf = smem + kOffV;
   uint8_t* const sb = smem + kOffSB;
-  float* const Am = reinterpret_cast<float*>(smem + kOffScr);
-  float* const Tt = Am + 64 * kLd;   // T^T: Tt[j * kLd + r] = T[r][j]
-  float* const Xt = Tt + 64 * kLd;   // X^T of the current block row: Xt[j * kXLd + t]
-  float* const Dm = Xt + 64 * kXLd;  // the diagonal blocks of T, row-major: Dm[(16 b + r) * kDLd + c]
-  uint8_t* const vn = smem + kOffScr;           // V_new^T bf16 [j][s]
-  uint8_t* const vnp = smem + kOffScr + 16384;  // V_new^T diag(exp(G_last - G)) bf16 [j][s]
-  uint8_t* const ost = smem + kOffScr;          // output rows bf16 [r][j]
-  uint8_t* const tpp = smem + kOffTpp;
-  uint8_t* const ntp = smem + kOffNtp;
-  uint8_t* const pm = smem + kOffPm;
 
-  ms.inv_tab[tid] = scale_inverse(scale_decode((uint32_t)tid, kMode));
+  if (tid < 256) ms.inv_tab[tid] = scale_inverse(scale_decode((uint32_t)tid, kMode));
   if (tid == 0) {
-    mbar_init(&ms.bar_stg[0], 1);
-    mbar_init(&ms.bar_stg[1], 1);
-    mbar_init(&ms.bar_mma, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ms.bar_kq[b], 1);
+      mbar_init(&ms.bar_p2[b], 2);
+      mbar_init(&ms.bar_hfree[b], 1);
+    }
+    mbar_init(&ms.bar_v, 1);
+    mbar_init(&ms.bar_p1, 1);
+    mbar_init(&ms.bar_cm, 1);
+    mbar_init(&ms.bar_seq, 1);
     fence_mbar_init();
   }
   if (warp == 0) tc::tmem_alloc(&ms.tmem_base, kTmemCols);
@@ -252,115 +302,433 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t T = ms.tmem_base;
-  const uint32_t id_kq = tc::idesc_bf16(128, 64);
-  const uint32_t id_yo = tc::idesc_bf16(128, 128);
-  const uint32_t id_u = tc::idesc_bf16(128, 64, true, false);
-  const uint32_t id_s = tc::idesc_bf16(128, 128, false, true);
-  const uint32_t id_tf = tc::idesc_tf32(128, 64);
-  const uint32_t id_mx = tc::idesc_mxf4nvf4(128, 128);
+  bool failed = false;
 
-  Cursor cur{(int32_t)blockIdx.x, 0, 0, 0, 0, 0};
-  cursor_seek(a, cur, tid == 0);
-  Cursor ahead = cur;  // next chunk to load
-  uint32_t pending = 0, stg_par = 0;  // bit b: stage b has a load in flight / its barrier's phase parity
-  int use_buf = 0;
-  // Queue the first two chunks.
-  for (int b = 0; b < 2; ++b) {
-    if (ahead.item < a.nitems) {
-      if (tid == 0) issue_chunk(a, smem + kOffStage + b * kStage, &ms.bar_stg[b], ahead, &tm_q, &tm_k, &tm_v);
-      pending |= 1u << b;
-      cursor_next(a, ahead, false);
-    }
-  }
-  float g_pre = 0.0f, b_pre = 0.0f;
-  if (tid < kC) load_gb(a, cur, tid, g_pre, b_pre);
+  if (warp < 8) {
+    // ================================== prep ==================================
+    float* const Am = reinterpret_cast<float*>(smem + kOffScr);
+    float* const Tt = Am + 64 * kLd;   // T^T: Tt[j * kLd + r] = T[r][j]
+    float* const Xt = Tt + 64 * kLd;   // X^T of the current block row: Xt[j * kXLd + t]
+    float* const Dm = Xt + 64 * kXLd;  // the diagonal blocks of T, row-major: Dm[(16 b + r) * kDLd + c]
+    uint8_t* const tpp = smem + kOffScr;  // T diag(beta), bf16 K-major [r][s], over A once A is consumed
+    const uint32_t id_kq = tc::idesc_bf16(128, 64);
+    const uint32_t id_u = tc::idesc_bf16(128, 64, true, false);
+    Cursor cur{(int32_t)blockIdx.x, 0, 0, 0, 0, 0};
+    cursor_seek(a, cur, false);
+    float g_pre = 0.0f, b_pre = 0.0f;
+    if (tid < kC) load_gb(a, cur, tid, g_pre, b_pre);
+    uint32_t g = 0, nseq = 0;
+    while (cur.item < a.nitems) {
+      const int b = g & 1;
+      uint8_t* const stage = smem + kOffKQ + b * kStageKQ;
+      Hand& hd = hand[b];
+      const bool last = (cur.chunk + 1) * kC >= cur.len;
 
-  bool mma_pending = false, failed = false;
-  uint32_t mma_par = 0;
-  auto mma_wait = [&]() -> bool {
-    mma_pending = true;
-    if (!mbar_wait_cta(&ms.bar_mma, mma_par)) return false;
-    mma_par ^= 1;
-    mma_pending = false;
-    tc::fence_after_sync();
-    return true;
-  };
-  auto sync_for_mma = [&]() {
-    tc::fence_smem_to_async();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-  };
-
-  int32_t slot = -1;
-  bool s_zero = true;  // the state is zero (not yet in TMEM / the bf16 copy)
-  while (cur.item < a.nitems) {
-    const int h = cur.h;
-    const int64_t t0 = cur.bos + cur.chunk * kC;
-    const int len = chunk_len(cur);
-    const bool last = (cur.chunk + 1) * kC >= cur.len;
-    uint8_t* const stage = smem + kOffStage + use_buf * kStage;
-
-    // ---- sequence start: slot and initial state ----
-    if (cur.chunk == 0) {
-      slot = a.slot_idx ? __ldg(a.slot_idx + cur.n) : -1;
-      if (slot >= a.num_slots) {
-        if (tid == 0) atomicOr(a.status, GDN_STATUS_BAD_SLOT);
-        slot = -1;
+      // ---- P1 = [K; Q] K^T as soon as the stage has landed ----
+      if (!group_wait(&ms.bar_kq[b], (g >> 1) & 1, tid == 0, kBarPrep)) { failed = true; break; }
+      if (tid == 0) {
+        tc::fence_after_sync();
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint64_t dk = stage_kmajor(stage, kStK0, ks);
+          tc::mma_bf16_ss(T + kColKQ, dk, dk, id_kq, ks > 0);  // rows 64..127 of A are Q's box
+        }
+        tc::commit(&ms.bar_p1);
       }
-      if (slot < 0) slot = -1;
-      const bool has = slot >= 0 && a.has_init && __ldg(a.has_init + cur.n) != 0;
-      s_zero = !has;
-      if (has) {
-        // Decode the NVFP4 tile straight into TMEM with one block-scaled MMA
-        // against the identity: D = I * S^T (lane j, column i).
-        const int64_t pt = (int64_t)slot * a.HV + h;
-        uint8_t* const codes = smem + kOffScr;
-        uint8_t* const ident = codes + kCodeBytes;
-        uint8_t* const sf = ident + kCodeBytes;
-        uint8_t* const sf_one = sf + kScaleBytes;
-        {
-          const int r = tid >> 1, c0 = 2 * (tid & 1);
-          const uint4* src = reinterpret_cast<const uint4*>(a.pool_codes + pt * kCodeBytes + r * 64 + 16 * c0);
-          const uint4 x0 = __ldg(src), x1 = __ldg(src + 1);
-          *reinterpret_cast<uint4*>(codes + 2048 * c0 + 16 * r) = x0;
-          *reinterpret_cast<uint4*>(codes + 2048 * (c0 + 1) + 16 * r) = x1;
-          const int t = tid >> 7, m0 = (tid & 127) >> 2, m1 = tid & 3;
-          reinterpret_cast<uint32_t*>(sf)[t * 128 + m0 * 4 + m1] =
-              __ldg(reinterpret_cast<const uint32_t*>(a.pool_scales + pt * kScaleBytes) + (32 * m1 + m0) * 2 + t);
-          reinterpret_cast<uint32_t*>(sf_one)[tid] = 0x38383838u;  // UE4M3 1.0
-          for (int e = tid; e < (int)kCodeBytes; e += kThreads) {
-            const int rr = e >> 6, byte = e & 63;
-            uint8_t val = 0;
-            if (2 * byte == rr) val = 0x02;      // E2M1 1.0, low nibble
-            if (2 * byte + 1 == rr) val = 0x20;  // high nibble
-            ident[canon(rr, byte)] = val;
+      // ---- gates (the hand-over buffer is free once the chain has finished chunk g - 2) ----
+      if (g >= 2 && !group_wait(&ms.bar_hfree[b], ((g - 2) >> 1) & 1, tid == 0, kBarPrep)) { failed = true; break; }
+      const float gv = g_pre, bv = b_pre;
+      if (tid < kC) {
+        float s = gv;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, s, o);
+          if (lane >= o) s += y;
+        }
+        ms.gw[tid] = s;
+        Cursor nx = cur;  // prefetch g, beta of the next chunk
+        cursor_next(a, nx, false);
+        load_gb(a, nx, tid, g_pre, b_pre);
+      }
+      group_sync(kBarPrep);
+      if (tid < kC) {
+        const float G = ms.gw[tid] + (tid >= 32 ? ms.gw[31] : 0.0f);
+        const float Glast = ms.gw[63] + ms.gw[31];
+        const float gm = __expf(G);
+        ms.G[tid] = G;
+        ms.bet[tid] = bv;
+        ms.bg[tid] = bv * gm;
+        ms.al[tid] = __expf(gv);
+        hd.de[tid] = __expf(Glast - G);
+        hd.qg[tid] = a.q_scale * gm;
+        if (tid == 0) hd.gC = __expf(Glast);
+      }
+      // ---- P1 done (and with it the previous chunk's P2: the v buffer and T diag(beta) are free) ----
+      if (!group_wait(&ms.bar_p1, g & 1, tid == 0, kBarPrep)) { failed = true; break; }
+      tc::fence_after_sync();
+      if (tid == 0) issue_v(a, vbuf, &ms.bar_v, cur, &tm_v);
+
+      // ---- A (strictly lower, for the solve) and P (lower incl. diagonal) ----
+      // The decay exp(G_r - G_s) of this thread's columns s in [sb0, sb0 + 32)
+      // comes from one exp at the last column s_hi <= r and a running product of
+      // per-token decays towards smaller s (exp(G_r - G_{s-1}) = exp(G_r - G_s)
+      // exp(g_s)): one exp per thread instead of one per element.
+      {
+        float vals[32];
+        tc::ld_32x32b_x32(T + lane_base + kColKQ + 32 * half, vals);
+        tc::ld_wait();
+        const int sb0 = 32 * half;
+        const bool arow = quad < 2;                  // rows 0-63: K K^T -> A; rows 64-127: Q K^T -> P
+        const int r = arow ? lrow : lrow - 64;
+        const int s_hi = arow ? r - 1 : r;           // last column kept
+        const float Gr = ms.G[r];
+        const float scale = arow ? ms.bet[r] : a.q_scale;
+        const int s_top = s_hi < sb0 + 31 ? s_hi : sb0 + 31;
+        float f = (s_top >= sb0) ? __expf(Gr - ms.G[s_top]) : 0.0f;
+        float alv[33];  // exp(g) of tokens sb0 .. sb0 + 32, in registers before the chain
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 t = *reinterpret_cast<const float4*>(ms.al + sb0 + 4 * c4);
+          alv[4 * c4] = t.x;
+          alv[4 * c4 + 1] = t.y;
+          alv[4 * c4 + 2] = t.z;
+          alv[4 * c4 + 3] = t.w;
+        }
+        alv[32] = half ? 1.0f : ms.al[32];  // token 64 does not exist (never used: s < s_top <= 63)
+#pragma unroll
+        for (int e = 31; e >= 0; --e) {
+          const int s = sb0 + e;
+          if (s < s_top) f *= alv[e + 1];
+          vals[e] = (s <= s_top) ? scale * vals[e] * f : 0.0f;
+        }
+        if (arow) {
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4)
+            *reinterpret_cast<float4*>(Am + r * kLd + sb0 + 4 * c4) =
+                make_float4(vals[4 * c4], vals[4 * c4 + 1], vals[4 * c4 + 2], vals[4 * c4 + 3]);
+        } else {
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8)
+            *reinterpret_cast<uint4*>(hd.pm + kbf16(r, sb0 + 8 * c8, 1024)) =
+                make_uint4(pack_bf16(vals[8 * c8], vals[8 * c8 + 1]), pack_bf16(vals[8 * c8 + 2], vals[8 * c8 + 3]),
+                           pack_bf16(vals[8 * c8 + 4], vals[8 * c8 + 5]), pack_bf16(vals[8 * c8 + 6], vals[8 * c8 + 7]));
+        }
+      }
+      tc::fence_before_sync();  // KQ is read before the next P1 overwrites it
+      group_sync(kBarPrep);
+      // ---- 2: T = (I + A)^-1 in 16 x 16 blocks ----
+      // T is kept transposed (a column of T is a contiguous row of Tt) so that
+      // the block products read both operands with 16-byte loads.
+      if (tid < 64) {
+        // diagonal blocks by forward substitution, one column per thread
+        const int b = tid >> 4, c = tid & 15;
+        float x[16];
+  #pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          const float4* arow = reinterpret_cast<const float4*>(Am + (16 * b + r) * kLd + 16 * b);
+          float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  #pragma unroll
+          for (int s4 = 0; s4 < (r + 3) / 4; ++s4) {
+            const float4 av = arow[s4];
+            const float aa[4] = {av.x, av.y, av.z, av.w};
+  #pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (4 * s4 + e < r) acc[e] = fmaf(aa[e], x[4 * s4 + e], acc[e]);
+          }
+          const float sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+          x[r] = (r < c) ? 0.0f : (r == c ? 1.0f : -sum);
+        }
+        float4* tcol = reinterpret_cast<float4*>(Tt + (16 * b + c) * kLd + 16 * b);
+  #pragma unroll
+        for (int r4 = 0; r4 < 4; ++r4) tcol[r4] = make_float4(x[4 * r4], x[4 * r4 + 1], x[4 * r4 + 2], x[4 * r4 + 3]);
+  #pragma unroll
+        for (int r = 0; r < 16; ++r) Dm[(16 * b + r) * kDLd + c] = x[r];
+      } else {
+        // zero the blocks above the diagonal: T[i][j] = Tt[j][i] with block(i) < block(j)
+        for (int e = tid - 64; e < 6 * 256; e += kGroup - 64) {
+          const int blk = e >> 8, idx = e & 255;
+          const int bi = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
+          const int bj = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
+          Tt[(16 * bj + (idx >> 4)) * kLd + 16 * bi + (idx & 15)] = 0.0f;
+        }
+      }
+      group_sync(kBarPrep);
+  #pragma unroll
+      for (int ib = 1; ib < 4; ++ib) {
+        const int r = tid & 15, jj = tid >> 4;
+        // X = A[block row ib][0 : 16 ib] T[0 : 16 ib][0 : 16 ib]  (column j of T is zero above row 16 m)
+  #pragma unroll
+        for (int m = 0; m < ib; ++m) {
+          const int j = jj + 16 * m;
+          const float4* arow = reinterpret_cast<const float4*>(Am + (16 * ib + r) * kLd);
+          const float4* tcol = reinterpret_cast<const float4*>(Tt + j * kLd);
+          float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  #pragma unroll
+          for (int k4 = 4 * m; k4 < 4 * ib; ++k4) {
+            const float4 av = arow[k4], tv = tcol[k4];
+            acc[0] = fmaf(av.x, tv.x, acc[0]);
+            acc[1] = fmaf(av.y, tv.y, acc[1]);
+            acc[2] = fmaf(av.z, tv.z, acc[2]);
+            acc[3] = fmaf(av.w, tv.w, acc[3]);
+          }
+          Xt[j * kXLd + r] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+        }
+        group_sync(kBarPrep);
+        // T[block row ib][0 : 16 ib] = -D_ib X
+  #pragma unroll
+        for (int m = 0; m < ib; ++m) {
+          const int j = jj + 16 * m;
+          const float4* drow = reinterpret_cast<const float4*>(Dm + (16 * ib + r) * kDLd);
+          const float4* xcol = reinterpret_cast<const float4*>(Xt + j * kXLd);
+          float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  #pragma unroll
+          for (int t4 = 0; t4 < 4; ++t4) {
+            const float4 dv = drow[t4], xv = xcol[t4];
+            acc[0] = fmaf(dv.x, xv.x, acc[0]);
+            acc[1] = fmaf(dv.y, xv.y, acc[1]);
+            acc[2] = fmaf(dv.z, xv.z, acc[2]);
+            acc[3] = fmaf(dv.w, xv.w, acc[3]);
+          }
+          Tt[j * kLd + 16 * ib + r] = -((acc[0] + acc[1]) + (acc[2] + acc[3]));
+        }
+        group_sync(kBarPrep);
+      }
+      // ---- T diag(beta) as bf16 (over A, consumed by the solve), -T diag(beta gamma) as fp32 ----
+#pragma unroll
+      for (int sp = 0; sp < 2; ++sp) {
+        const int r = tid & 63, s8 = 2 * (tid >> 6) + sp;
+        float tv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) tv[e] = Tt[(8 * s8 + e) * kLd + r];
+        uint32_t pb[4];
+        float nt[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) nt[e] = -tv[e] * ms.bg[8 * s8 + e];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          pb[e] = pack_bf16(tv[2 * e] * ms.bet[8 * s8 + 2 * e], tv[2 * e + 1] * ms.bet[8 * s8 + 2 * e + 1]);
+        *reinterpret_cast<uint4*>(tpp + kbf16(r, 8 * s8, 1024)) = make_uint4(pb[0], pb[1], pb[2], pb[3]);
+        *reinterpret_cast<float4*>(hd.ntp + kf32(r, 8 * s8, 2048)) = make_float4(nt[0], nt[1], nt[2], nt[3]);
+        *reinterpret_cast<float4*>(hd.ntp + kf32(r, 8 * s8 + 4, 2048)) = make_float4(nt[4], nt[5], nt[6], nt[7]);
+      }
+      tc::fence_smem_to_async();
+      // ---- v landed: P2 into U[b] (free since bar_hfree above); hand over to the chain ----
+      if (!group_wait(&ms.bar_v, g & 1, tid == 0, kBarPrep)) { failed = true; break; }
+      if (tid == 0) {
+        tc::fence_after_sync();
+        // P2: U^T = V^T T''^T  (A = V as MN-major, M = d_v, N = C, K = C)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_bf16_ss(T + kColU + 64 * b, tc::smem_desc_sw128(vbuf + kV0 + 2048 * ks, kBox, 1024),
+                          tc::smem_desc(tpp + 256 * ks, 128, 1024), id_u, ks > 0);
+        mbar_arrive(&ms.bar_p2[b]);  // the hand-over (written before the barrier above) is published
+        tc::commit(&ms.bar_p2[b]);
+      }
+      if (last) {
+        // the chain transposes the final state through this group's scratch: wait for it
+        if (!group_wait(&ms.bar_seq, nseq & 1, tid == 0, kBarPrep)) { failed = true; break; }
+        ++nseq;
+      }
+      ++g;
+      cursor_next(a, cur, false);
+    }
+  } else {
+    // ================================== chain ==================================
+    const int ctid = tid - kGroup;  // 0..255
+    const uint32_t id_yo = tc::idesc_bf16(128, 128);
+    const uint32_t id_o2 = tc::idesc_bf16(128, 64);
+    const uint32_t id_s = tc::idesc_bf16(128, 128, false, true);
+    const uint32_t id_tf = tc::idesc_tf32(128, 64);
+    const uint32_t id_mx = tc::idesc_mxf4nvf4(128, 128);
+    const int64_t row_stride = (int64_t)a.HV * kD;
+    Cursor cur{(int32_t)blockIdx.x, 0, 0, 0, 0, 0};
+    cursor_seek(a, cur, ctid == 0);
+    Cursor ahead = cur;  // next chunk whose k/q to load
+    for (int b = 0; b < 2; ++b) {
+      if (ahead.item < a.nitems) {
+        if (ctid == 0) issue_kq(a, smem + kOffKQ + b * kStageKQ, &ms.bar_kq[b], ahead, &tm_q, &tm_k);
+        cursor_next(a, ahead, false);
+      }
+    }
+    uint32_t g = 0, cm_par = 0;
+    int32_t slot = -1;
+    bool s_zero = true;  // the state is zero (not yet in TMEM / the bf16 copy)
+    auto cm_wait = [&]() -> bool {
+      const bool ok = group_wait(&ms.bar_cm, cm_par, ctid == 0, kBarChain);
+      cm_par ^= 1u;
+      tc::fence_after_sync();
+      return ok;
+    };
+    while (cur.item < a.nitems) {
+      const int b = g & 1;
+      uint8_t* const stage = smem + kOffKQ + b * kStageKQ;
+      Hand& hd = hand[b];
+      const int h = cur.h;
+      const int64_t t0 = cur.bos + cur.chunk * kC;
+      const int len = chunk_len(cur);
+      const bool last = (cur.chunk + 1) * kC >= cur.len;
+      const uint32_t ub = T + kColU + 64 * b;
+
+      // ---- sequence start: slot and initial state ----
+      if (cur.chunk == 0) {
+        bool has = false;
+        slot = seq_slot(a, cur.n, ctid == 0, has);
+        s_zero = !has;
+        if (has) {
+          // Decode the NVFP4 tile straight into TMEM with one block-scaled MMA
+          // against the identity: D = I * S^T (lane j, column i).
+          const int64_t pt = (int64_t)slot * a.HV + h;
+          uint8_t* const codes = sb;
+          uint8_t* const ident = codes + kCodeBytes;
+          uint8_t* const sf = ident + kCodeBytes;
+          uint8_t* const sf_one = sf + kScaleBytes;
+          {
+            const int r = ctid >> 1, c0 = 2 * (ctid & 1);
+            const uint4* src = reinterpret_cast<const uint4*>(a.pool_codes + pt * kCodeBytes + r * 64 + 16 * c0);
+            const uint4 x0 = __ldg(src), x1 = __ldg(src + 1);
+            *reinterpret_cast<uint4*>(codes + 2048 * c0 + 16 * r) = x0;
+            *reinterpret_cast<uint4*>(codes + 2048 * (c0 + 1) + 16 * r) = x1;
+            const int t = ctid >> 7, m0 = (ctid & 127) >> 2, m1 = ctid & 3;
+            reinterpret_cast<uint32_t*>(sf)[t * 128 + m0 * 4 + m1] =
+                __ldg(reinterpret_cast<const uint32_t*>(a.pool_scales + pt * kScaleBytes) + (32 * m1 + m0) * 2 + t);
+            reinterpret_cast<uint32_t*>(sf_one)[ctid] = 0x38383838u;  // UE4M3 1.0
+            for (int e = ctid; e < (int)kCodeBytes; e += kGroup) {
+              const int rr = e >> 6, byte = e & 63;
+              uint8_t val = 0;
+              if (2 * byte == rr) val = 0x02;      // E2M1 1.0, low nibble
+              if (2 * byte + 1 == rr) val = 0x20;  // high nibble
+              ident[canon(rr, byte)] = val;
+            }
+          }
+          const float gs = __ldg(a.pool_gs + pt);
+          tc::fence_smem_to_async();
+          tc::fence_before_sync();
+          group_sync(kBarChain);
+          if (ctid == 0) {
+            tc::fence_after_sync();
+            for (int t = 0; t < 2; ++t) {
+              tc::cp_32x128b_warpx4(T + kColSF + 4 * t, tc::smem_desc(sf + 512 * t, 0, 128));
+              tc::cp_32x128b_warpx4(T + kColOne + 4 * t, tc::smem_desc(sf_one + 512 * t, 0, 128));
+            }
+            for (int t = 0; t < 2; ++t)
+              tc::mma_mxf4nvf4(T + kColS, tc::smem_desc(ident + 4096 * t, 2048, 128),
+                               tc::smem_desc(codes + 4096 * t, 2048, 128), id_mx, T + kColOne + 4 * t,
+                               T + kColSF + 4 * t, t > 0);
+            tc::commit(&ms.bar_cm);
+          }
+          if (!cm_wait()) { failed = true; break; }
+          // S *= gs in TMEM; the bf16 copy for the state products (over the decode operands)
+          float sv[32];
+#pragma unroll
+          for (int p = 0; p < 2; ++p) {
+            const uint32_t ta = T + lane_base + kColS + 64 * half + 32 * p;
+            tc::ld_32x32b_x32(ta, sv);
+            tc::ld_wait();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) sv[c] *= gs;
+            tc::st_32x32b_x32(ta, sv);
+            group_sync(kBarChain);  // every thread's reads of the decode operands precede the overwrite
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8) {
+              const int i = 64 * half + 32 * p + 8 * c8;
+              *reinterpret_cast<uint4*>(sb + kbf16(lrow, i, 2048)) =
+                  make_uint4(pack_bf16(sv[8 * c8], sv[8 * c8 + 1]), pack_bf16(sv[8 * c8 + 2], sv[8 * c8 + 3]),
+                             pack_bf16(sv[8 * c8 + 4], sv[8 * c8 + 5]), pack_bf16(sv[8 * c8 + 6], sv[8 * c8 + 7]));
+            }
+          }
+          tc::st_wait();
+          tc::fence_smem_to_async();
+          tc::fence_before_sync();
+          group_sync(kBarChain);
+        }
+      }
+      const bool s0 = s_zero;
+
+      // ---- Y | O1 = S^T [K; Q]^T once the stage has landed ----
+      if (!group_wait(&ms.bar_kq[b], (g >> 1) & 1, ctid == 0, kBarChain)) { failed = true; break; }
+      if (ctid == 0 && !s0) {
+        tc::fence_after_sync();
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          tc::mma_bf16_ss(T + kColY, tc::smem_desc(sb + 256 * ks, 128, 2048), stage_kmajor(stage, kStK0, ks), id_yo,
+                          ks > 0);
+      }
+      // ---- the prep group's hand-over: P4, V_new^T = U^T + Y (-T')^T ----
+      if (!group_wait(&ms.bar_p2[b], (g >> 1) & 1, ctid == 0, kBarChain)) { failed = true; break; }
+      if (ctid == 0) {
+        tc::fence_after_sync();
+        if (!s0) {
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            tc::mma_tf32_ts(ub, T + kColY + 8 * ks, tc::smem_desc(hd.ntp + 256 * ks, 128, 2048), id_tf, 1);
+        }
+        tc::commit(&ms.bar_cm);
+      }
+      if (!cm_wait()) { failed = true; break; }
+
+      // ---- V_new^T -> bf16 [V_new^T | V_new^T diag(exp(G_last - G))] in U[b]; decay the state ----
+      {
+        float vals[32];
+        tc::ld_32x32b_x32(ub + lane_base + 32 * half, vals);
+        tc::ld_wait();
+        uint32_t wn[16], wd[16];
+#pragma unroll
+        for (int p = 0; p < 16; ++p) {
+          const int s = 32 * half + 2 * p;
+          wn[p] = pack_bf16(vals[2 * p], vals[2 * p + 1]);
+          wd[p] = pack_bf16(vals[2 * p] * hd.de[s], vals[2 * p + 1] * hd.de[s + 1]);
+        }
+        tc::fence_before_sync();
+        group_sync(kBarChain);  // every lane's V_new^T is read before U[b] is overwritten
+        tc::fence_after_sync();
+        tc::st_32x32b_x16(ub + lane_base + 16 * half, wn);
+        tc::st_32x32b_x16(ub + lane_base + 32 + 16 * half, wd);
+        if (!s0) {
+          const float gC = hd.gC;
+          float sv[32];
+#pragma unroll
+          for (int p = 0; p < 2; ++p) {
+            const uint32_t ta = T + lane_base + kColS + 64 * half + 32 * p;
+            tc::ld_32x32b_x32(ta, sv);
+            tc::ld_wait();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) sv[c] *= gC;
+            tc::st_32x32b_x32(ta, sv);
           }
         }
-        const float gs = __ldg(a.pool_gs + pt);
-        sync_for_mma();
-        if (tid == 0) {
-          for (int t = 0; t < 2; ++t) {
-            tc::cp_32x128b_warpx4(T + kColSF + 4 * t, tc::smem_desc(sf + 512 * t, 0, 128));
-            tc::cp_32x128b_warpx4(T + kColOne + 4 * t, tc::smem_desc(sf_one + 512 * t, 0, 128));
-          }
-          for (int t = 0; t < 2; ++t)
-            tc::mma_mxf4nvf4(T + kColS, tc::smem_desc(ident + 4096 * t, 2048, 128),
-                             tc::smem_desc(codes + 4096 * t, 2048, 128), id_mx, T + kColOne + 4 * t,
-                             T + kColSF + 4 * t, t > 0);
-          tc::commit(&ms.bar_mma);
-        }
-        if (!mma_wait()) { failed = true; break; }
-        // S *= gs in TMEM; the bf16 copy for the state products
+        tc::st_wait();
+      }
+      tc::fence_before_sync();
+      group_sync(kBarChain);
+      if (ctid == 0) {
+        tc::fence_after_sync();
+        // P6: O2 = V_new^T P^T  (A = V_new^T bf16 in TMEM, M = d_v, N = C, K = C)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_bf16_ts(T + kColO2, ub + 8 * ks, tc::smem_desc(hd.pm + 256 * ks, 128, 1024), id_o2, ks > 0);
+        // P7: S^T += V_new'^T K  (A in TMEM, B = K as MN-major, N = d_k)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_bf16_ts(T + kColS, ub + 32 + 8 * ks, tc::smem_desc_sw128(stage + kStK0 + 2048 * ks, 2 * kBox, 1024),
+                          id_s, !s0 || ks > 0);
+        tc::commit(&ms.bar_cm);
+        tc::commit(&ms.bar_hfree[b]);  // the hand-over and U[b] are free once these complete
+      }
+      if (!cm_wait()) { failed = true; break; }
+      s_zero = false;
+      // The stage is free: queue the chunk after next into it.
+      if (ahead.item < a.nitems) {
+        if (ctid == 0) issue_kq(a, stage, &ms.bar_kq[b], ahead, &tm_q, &tm_k);
+        cursor_next(a, ahead, false);
+      }
+
+      // ---- bf16 copy of the updated state for the next chunk's state products ----
+      if (!last) {
         float sv[32];
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
-          const uint32_t ta = T + lane_base + kColS + 64 * half + 32 * p;
-          tc::ld_32x32b_x32(ta, sv);
+          tc::ld_32x32b_x32(T + lane_base + kColS + 64 * half + 32 * p, sv);
           tc::ld_wait();
-#pragma unroll
-          for (int c = 0; c < 32; ++c) sv[c] *= gs;
-          tc::st_32x32b_x32(ta, sv);
 #pragma unroll
           for (int c8 = 0; c8 < 4; ++c8) {
             const int i = 64 * half + 32 * p + 8 * c8;
@@ -369,380 +737,87 @@ __global__ void __launch_bounds__(kThreads, 1)
                            pack_bf16(sv[8 * c8 + 4], sv[8 * c8 + 5]), pack_bf16(sv[8 * c8 + 6], sv[8 * c8 + 7]));
           }
         }
-        tc::st_wait();
-        sync_for_mma();
+        tc::fence_smem_to_async();
       }
-    }
+      // ---- outputs O = diag(q_scale gamma) O1 + O2 -> bf16, straight to global (lanes j: 64-byte rows) ----
+#pragma unroll
+      for (int hc = 0; hc < 2; ++hc) {
+        float v2[16], v1[16];
+        const uint32_t col = 32 * half + 16 * hc;
+        tc::ld_32x32b_x16(T + lane_base + kColO2 + col, v2);
+        if (!s0) tc::ld_32x32b_x16(T + lane_base + kColO1 + col, v1);
+        tc::ld_wait();
+        __nv_bfloat16* orow = a.out + (t0 + col) * row_stride + (int64_t)h * kD + lrow;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const int r = col + c;
+          const float o = s0 ? v2[c] : fmaf(hd.qg[r], v1[c], v2[c]);
+          if (r < len) *orow = __float2bfloat16_rn(o);
+          orow += row_stride;
+        }
+      }
+      tc::fence_before_sync();
+      group_sync(kBarChain);  // the bf16 state copy is complete and O1, O2 are read
 
-    // ---- 0: stage ready -> P1, Y, O1 on the tensor cores; decay prefix ----
-    if (!mbar_wait_cta(&ms.bar_stg[use_buf], (stg_par >> use_buf) & 1u)) { failed = true; break; }
-    stg_par ^= 1u << use_buf;
-    pending &= ~(1u << use_buf);
-    const bool s0 = s_zero;
-    if (tid == 0) {
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint64_t dk = stage_kmajor(stage, kStK0, ks);
-        tc::mma_bf16_ss(T + kColKQ, dk, dk, id_kq, ks > 0);  // [K; Q] K^T: rows 64..127 are Q's box
-      }
-      if (!s0) {
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint64_t ds = tc::smem_desc(sb + 256 * ks, 128, 2048);
-          tc::mma_bf16_ss(T + kColY, ds, stage_kmajor(stage, kStK0, ks), id_yo, ks > 0);  // [Y | O1]
-        }
-      }
-      tc::commit(&ms.bar_mma);
-    }
-    const float gv = g_pre, bv = b_pre;
-    if (tid < kC) {
-      float s = gv;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, s, o);
-        if (lane >= o) s += y;
-      }
-      ms.gw[tid] = s;
-      // prefetch g, beta of the next chunk
-      Cursor nx = cur;
-      cursor_next(a, nx, false);
-      load_gb(a, nx, tid, g_pre, b_pre);
-    }
-    __syncthreads();
-    if (tid < kC) {
-      const float G = ms.gw[tid] + (tid >= 32 ? ms.gw[31] : 0.0f);
-      const float Glast = ms.gw[63] + ms.gw[31];
-      const float gm = __expf(G);
-      ms.G[tid] = G;
-      ms.bet[tid] = bv;
-      ms.bg[tid] = bv * gm;
-      ms.de[tid] = __expf(Glast - G);
-      ms.qg[tid] = a.q_scale * gm;
-      ms.al[tid] = __expf(gv);
-    }
-    if (!mma_wait()) { failed = true; break; }  // also publishes G, bet, bg, de, qg
-
-    // ---- 1: A (strictly lower, for the solve) and P (lower incl. diagonal) ----
-    // The decay exp(G_r - G_s) of this thread's columns s in [sb0, sb0 + 32)
-    // comes from one exp at the last column s_hi <= r and a running product of
-    // per-token decays towards smaller s (exp(G_r - G_{s-1}) = exp(G_r - G_s)
-    // exp(g_s)): one exp per thread instead of one per element.
-    {
-      float vals[32];
-      tc::ld_32x32b_x32(T + lane_base + kColKQ + 32 * half, vals);
-      tc::ld_wait();
-      const int sb0 = 32 * half;
-      const bool arow = quad < 2;                  // rows 0-63: K K^T -> A; rows 64-127: Q K^T -> P
-      const int r = arow ? lrow : lrow - 64;
-      const int s_hi = arow ? r - 1 : r;           // last column kept
-      const float Gr = ms.G[r];
-      const float scale = arow ? ms.bet[r] : a.q_scale;
-      const int s_top = s_hi < sb0 + 31 ? s_hi : sb0 + 31;
-      float f = (s_top >= sb0) ? __expf(Gr - ms.G[s_top]) : 0.0f;
-      // exp(g) of tokens sb0 + 1 .. sb0 + 32, in registers before the chain
-      float alv[33];
-#pragma unroll
-      for (int c4 = 0; c4 < 8; ++c4) {
-        const float4 t = *reinterpret_cast<const float4*>(ms.al + sb0 + 4 * c4);
-        alv[4 * c4] = t.x;
-        alv[4 * c4 + 1] = t.y;
-        alv[4 * c4 + 2] = t.z;
-        alv[4 * c4 + 3] = t.w;
-      }
-      alv[32] = half ? 1.0f : ms.al[32];  // token 64 does not exist (never used: s < s_top <= 63)
-      float o[32];
-#pragma unroll
-      for (int e = 31; e >= 0; --e) {
-        const int s = sb0 + e;
-        if (s < s_top) f *= alv[e + 1];
-        o[e] = (s <= s_top) ? scale * vals[e] * f : 0.0f;
-      }
-      if (arow) {
-#pragma unroll
-        for (int c4 = 0; c4 < 8; ++c4)
-          *reinterpret_cast<float4*>(Am + r * kLd + sb0 + 4 * c4) =
-              make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
-      } else {
-#pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8)
-          *reinterpret_cast<uint4*>(pm + kbf16(r, sb0 + 8 * c8, 1024)) =
-              make_uint4(pack_bf16(o[8 * c8], o[8 * c8 + 1]), pack_bf16(o[8 * c8 + 2], o[8 * c8 + 3]),
-                         pack_bf16(o[8 * c8 + 4], o[8 * c8 + 5]), pack_bf16(o[8 * c8 + 6], o[8 * c8 + 7]));
-      }
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-
-    // ---- 2: T = (I + A)^-1 in 16 x 16 blocks ----
-    // T is kept transposed (a column of T is a contiguous row of Tt) so that
-    // the block products read both operands with 16-byte loads.
-    if (tid < 64) {
-      // diagonal blocks by forward substitution, one column per thread
-      const int b = tid >> 4, c = tid & 15;
-      float x[16];
-#pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        const float4* arow = reinterpret_cast<const float4*>(Am + (16 * b + r) * kLd + 16 * b);
-        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-        for (int s4 = 0; s4 < (r + 3) / 4; ++s4) {
-          const float4 av = arow[s4];
-          const float aa[4] = {av.x, av.y, av.z, av.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            if (4 * s4 + e < r) acc[e] = fmaf(aa[e], x[4 * s4 + e], acc[e]);
-        }
-        const float sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-        x[r] = (r < c) ? 0.0f : (r == c ? 1.0f : -sum);
-      }
-      float4* tcol = reinterpret_cast<float4*>(Tt + (16 * b + c) * kLd + 16 * b);
-#pragma unroll
-      for (int r4 = 0; r4 < 4; ++r4) tcol[r4] = make_float4(x[4 * r4], x[4 * r4 + 1], x[4 * r4 + 2], x[4 * r4 + 3]);
-#pragma unroll
-      for (int r = 0; r < 16; ++r) Dm[(16 * b + r) * kDLd + c] = x[r];
-    } else {
-      // zero the blocks above the diagonal: T[i][j] = Tt[j][i] with block(i) < block(j)
-      for (int e = tid - 64; e < 6 * 256; e += kThreads - 64) {
-        const int blk = e >> 8, idx = e & 255;
-        const int bi = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
-        const int bj = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
-        Tt[(16 * bj + (idx >> 4)) * kLd + 16 * bi + (idx & 15)] = 0.0f;
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int ib = 1; ib < 4; ++ib) {
-      const int r = tid & 15, jj = tid >> 4;
-      // X = A[block row ib][0 : 16 ib] T[0 : 16 ib][0 : 16 ib]  (column j of T is zero above row 16 m)
-#pragma unroll
-      for (int m = 0; m < ib; ++m) {
-        const int j = jj + 16 * m;
-        const float4* arow = reinterpret_cast<const float4*>(Am + (16 * ib + r) * kLd);
-        const float4* tcol = reinterpret_cast<const float4*>(Tt + j * kLd);
-        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-        for (int k4 = 4 * m; k4 < 4 * ib; ++k4) {
-          const float4 av = arow[k4], tv = tcol[k4];
-          acc[0] = fmaf(av.x, tv.x, acc[0]);
-          acc[1] = fmaf(av.y, tv.y, acc[1]);
-          acc[2] = fmaf(av.z, tv.z, acc[2]);
-          acc[3] = fmaf(av.w, tv.w, acc[3]);
-        }
-        Xt[j * kXLd + r] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-      }
-      __syncthreads();
-      // T[block row ib][0 : 16 ib] = -D_ib X
-#pragma unroll
-      for (int m = 0; m < ib; ++m) {
-        const int j = jj + 16 * m;
-        const float4* drow = reinterpret_cast<const float4*>(Dm + (16 * ib + r) * kDLd);
-        const float4* xcol = reinterpret_cast<const float4*>(Xt + j * kXLd);
-        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-        for (int t4 = 0; t4 < 4; ++t4) {
-          const float4 dv = drow[t4], xv = xcol[t4];
-          acc[0] = fmaf(dv.x, xv.x, acc[0]);
-          acc[1] = fmaf(dv.y, xv.y, acc[1]);
-          acc[2] = fmaf(dv.z, xv.z, acc[2]);
-          acc[3] = fmaf(dv.w, xv.w, acc[3]);
-        }
-        Tt[j * kLd + 16 * ib + r] = -((acc[0] + acc[1]) + (acc[2] + acc[3]));
-      }
-      __syncthreads();
-    }
-    // T diag(beta) as bf16, -T diag(beta gamma) as fp32: B operands ([r][s], K = s)
-#pragma unroll
-    for (int sp = 0; sp < 2; ++sp) {
-      const int r = tid & 63, s8 = 2 * (tid >> 6) + sp;
-      float tv[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) tv[e] = Tt[(8 * s8 + e) * kLd + r];
-      uint32_t pb[4];
-      float nt[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) nt[e] = -tv[e] * ms.bg[8 * s8 + e];
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        pb[e] = pack_bf16(tv[2 * e] * ms.bet[8 * s8 + 2 * e], tv[2 * e + 1] * ms.bet[8 * s8 + 2 * e + 1]);
-      *reinterpret_cast<uint4*>(tpp + kbf16(r, 8 * s8, 1024)) = make_uint4(pb[0], pb[1], pb[2], pb[3]);
-      *reinterpret_cast<float4*>(ntp + kf32(r, 8 * s8, 2048)) = make_float4(nt[0], nt[1], nt[2], nt[3]);
-      *reinterpret_cast<float4*>(ntp + kf32(r, 8 * s8 + 4, 2048)) = make_float4(nt[4], nt[5], nt[6], nt[7]);
-    }
-    sync_for_mma();
-    if (tid == 0) {
-      // P2: U^T = V^T T''^T  (A = V as MN-major, M = d_v, N = C, K = C)
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        tc::mma_bf16_ss(T + kColU, tc::smem_desc_sw128(stage + kStV0 + 2048 * ks, kBox, 1024),
-                        tc::smem_desc(tpp + 256 * ks, 128, 1024), id_u, ks > 0);
-      if (!s0) {
-        // P4: V_new^T = U^T + Y (-T')^T  (tf32, A = Y from TMEM)
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          tc::mma_tf32_ts(T + kColU, T + kColY + 8 * ks, tc::smem_desc(ntp + 256 * ks, 128, 2048), id_tf, 1);
-      }
-      tc::commit(&ms.bar_mma);
-    }
-    if (!mma_wait()) { failed = true; break; }
-
-    // ---- 3: V_new^T -> operands; decay the state ----
-    {
-      float vals[32];
-      tc::ld_32x32b_x32(T + lane_base + kColU + 32 * half, vals);
-      tc::ld_wait();
-      const int j = lrow, sb0 = 32 * half;
-#pragma unroll
-      for (int c8 = 0; c8 < 4; ++c8) {
-        uint32_t w[4], wd[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c = 8 * c8 + 2 * e;
-          w[e] = pack_bf16(vals[c], vals[c + 1]);
-          wd[e] = pack_bf16(vals[c] * ms.de[sb0 + c], vals[c + 1] * ms.de[sb0 + c + 1]);
-        }
-        *reinterpret_cast<uint4*>(vn + kbf16(j, sb0 + 8 * c8, 1024)) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4*>(vnp + kbf16(j, sb0 + 8 * c8, 1024)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
-      }
-      if (!s0) {
-        const float gC = __expf(ms.G[kC - 1]);
+      // ---- sequence end: requantise the state into its slot (through the prep scratch, which is idle) ----
+      if (last) {
+        float* F = reinterpret_cast<float*>(smem + kOffSB);
         float sv[32];
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
-          const uint32_t ta = T + lane_base + kColS + 64 * half + 32 * p;
-          tc::ld_32x32b_x32(ta, sv);
+          tc::ld_32x32b_x32(T + lane_base + kColS + 64 * half + 32 * p, sv);
           tc::ld_wait();
 #pragma unroll
-          for (int c = 0; c < 32; ++c) sv[c] *= gC;
-          tc::st_32x32b_x32(ta, sv);
+          for (int c = 0; c < 32; ++c) F[(64 * half + 32 * p + c) * kFPitch + lrow] = sv[c];
         }
-        tc::st_wait();
-      }
-    }
-    sync_for_mma();
-    if (tid == 0) {
-      // P6: O2 = V_new^T P^T  (M = d_v, N = C, K = C)
+        tc::fence_before_sync();
+        group_sync(kBarChain);
+        if (slot >= 0) {
+          const int i = ctid & 127, hh = ctid >> 7;
+          float2 x[32];
+          const float4* src = reinterpret_cast<const float4*>(F + i * kFPitch + 64 * hh);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        tc::mma_bf16_ss(T + kColO2, tc::smem_desc(vn + 256 * ks, 128, 1024), tc::smem_desc(pm + 256 * ks, 128, 1024),
-                        id_kq, ks > 0);
-      // P7: S^T += V_new'^T K  (B = K as MN-major, N = d_k)
+          for (int p = 0; p < 16; ++p) {
+            const float4 f = src[p];
+            x[2 * p] = make_float2(f.x, f.y);
+            x[2 * p + 1] = make_float2(f.z, f.w);
+          }
+          float am[4];
+          float tmax = block_amax4(x, am);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        tc::mma_bf16_ss(T + kColS, tc::smem_desc(vnp + 256 * ks, 128, 1024),
-                        tc::smem_desc_sw128(stage + kStK0 + 2048 * ks, 2 * kBox, 1024), id_s, !s0 || ks > 0);
-      tc::commit(&ms.bar_mma);
-    }
-    if (!mma_wait()) { failed = true; break; }
-    s_zero = false;
-    // The stage is free: queue the next chunk to load into it.
-    if (ahead.item < a.nitems) {
-      if (tid == 0) issue_chunk(a, stage, &ms.bar_stg[use_buf], ahead, &tm_q, &tm_k, &tm_v);
-      pending |= 1u << use_buf;
-      cursor_next(a, ahead, false);
-    }
-    use_buf ^= 1;
-
-    // ---- 4: outputs O = diag(q_scale gamma) O1 + O2 -> bf16 rows ----
-    {
-      float v2[32], v1[32];
-      tc::ld_32x32b_x32(T + lane_base + kColO2 + 32 * half, v2);
-      if (!s0) tc::ld_32x32b_x32(T + lane_base + kColO1 + 32 * half, v1);
-      tc::ld_wait();
-      const int j = lrow;
+          for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+          if (lane == 0) ms.amax[warp - 8] = tmax;
+          group_sync(kBarChain);
+          float amax = ms.amax[0];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const int r = 32 * half + c;
-        const float o = s0 ? v2[c] : fmaf(ms.qg[r], v1[c], v2[c]);
-        *reinterpret_cast<__nv_bfloat16*>(ost + r * kOPitch + 2 * j) = __float2bfloat16_rn(o);
-      }
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    {
-      const int64_t row_stride = (int64_t)a.HV * kD;
-#pragma unroll
-      for (int it = 0; it < 4; ++it) {
-        const int e = tid + kThreads * it;
-        const int r = e >> 4, c16 = e & 15;
-        if (r < len)
-          *reinterpret_cast<uint4*>(a.out + (t0 + r) * row_stride + (int64_t)h * kD + 8 * c16) =
-              *reinterpret_cast<const uint4*>(ost + r * kOPitch + 16 * c16);
-      }
-    }
-
-    if (!last) {
-      // bf16 copy of the updated state for the next chunk's state products
-      float sv[32];
-#pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        tc::ld_32x32b_x32(T + lane_base + kColS + 64 * half + 32 * p, sv);
-        tc::ld_wait();
-#pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
-          const int i = 64 * half + 32 * p + 8 * c8;
-          *reinterpret_cast<uint4*>(sb + kbf16(lrow, i, 2048)) =
-              make_uint4(pack_bf16(sv[8 * c8], sv[8 * c8 + 1]), pack_bf16(sv[8 * c8 + 2], sv[8 * c8 + 3]),
-                         pack_bf16(sv[8 * c8 + 4], sv[8 * c8 + 5]), pack_bf16(sv[8 * c8 + 6], sv[8 * c8 + 7]));
+          for (int w = 1; w < 8; ++w) amax = fmaxf(amax, ms.amax[w]);
+          const float gs_new = (amax > 0.0f) ? __fdiv_rn(amax, a.gden) : 1.0f;
+          const int64_t pt = (int64_t)slot * a.HV + h;
+          uint32_t words[8], scw;
+          requant_half_row<kMode>(
+              x, am, __frcp_rn(gs_new), ms.inv_tab, words, scw,
+              a.debug_y ? a.debug_y + (((int64_t)cur.n * a.HV + h) * kD + i) * kD + 64 * hh : nullptr);
+          uint4* dst = reinterpret_cast<uint4*>(a.pool_codes + pt * kCodeBytes + i * 64 + 32 * hh);
+          dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
+          dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
+          *reinterpret_cast<uint32_t*>(a.pool_scales + pt * kScaleBytes + i * 8 + 4 * hh) = scw;
+          if (ctid == 0) a.pool_gs[pt] = gs_new;
         }
+        group_sync(kBarChain);  // the transpose buffer is read
+        if (ctid == 0) mbar_arrive(&ms.bar_seq);  // the prep group's scratch is free again
       }
-      sync_for_mma();  // also: output staging read before the next chunk reuses it
-    } else {
-      // ---- sequence end: requantise the state into its slot ----
-      float* F = reinterpret_cast<float*>(smem + kOffSB);
-      __syncthreads();  // output staging read (it overlaps F)
-      float sv[32];
-#pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        tc::ld_32x32b_x32(T + lane_base + kColS + 64 * half + 32 * p, sv);
-        tc::ld_wait();
-#pragma unroll
-        for (int c = 0; c < 32; ++c) F[(64 * half + 32 * p + c) * kFPitch + lrow] = sv[c];
-      }
-      tc::fence_before_sync();
-      __syncthreads();
-      if (slot >= 0) {
-        const int i = tid & 127, hh = tid >> 7;
-        float2 x[32];
-        const float4* src = reinterpret_cast<const float4*>(F + i * kFPitch + 64 * hh);
-#pragma unroll
-        for (int p = 0; p < 16; ++p) {
-          const float4 f = src[p];
-          x[2 * p] = make_float2(f.x, f.y);
-          x[2 * p + 1] = make_float2(f.z, f.w);
-        }
-        float am[4];
-        float tmax = block_amax4(x, am);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
-        if (lane == 0) ms.amax[warp] = tmax;
-        __syncthreads();
-        float amax = ms.amax[0];
-#pragma unroll
-        for (int w = 1; w < kWarps; ++w) amax = fmaxf(amax, ms.amax[w]);
-        const float gs_new = (amax > 0.0f) ? __fdiv_rn(amax, a.gden) : 1.0f;
-        const int64_t pt = (int64_t)slot * a.HV + h;
-        uint32_t words[8], scw;
-        requant_half_row<kMode>(
-            x, am, __frcp_rn(gs_new), ms.inv_tab, words, scw,
-            a.debug_y ? a.debug_y + (((int64_t)cur.n * a.HV + h) * kD + i) * kD + 64 * hh : nullptr);
-        uint4* dst = reinterpret_cast<uint4*>(a.pool_codes + pt * kCodeBytes + i * 64 + 32 * hh);
-        dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
-        dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
-        *reinterpret_cast<uint32_t*>(a.pool_scales + pt * kScaleBytes + i * 8 + 4 * hh) = scw;
-        if (tid == 0) a.pool_gs[pt] = gs_new;
-      }
-      __syncthreads();  // the transpose buffer is free again
+      ++g;
+      cursor_next(a, cur, ctid == 0);
     }
-    cursor_next(a, cur, tid == 0);
   }
 
-  if (failed && tid == 0) {
-    // Report, then give the copies and MMAs still queued a bounded chance to
+  if (failed && (tid == 0 || tid == kGroup)) {
+    // Report, then give the copies and MMAs still queued a bounded time to
     // finish before the shared and tensor memory are released.
     atomicOr(a.status, kStatusWaitTimeout);
-    for (int b = 0; b < 2; ++b)
-      if ((pending >> b) & 1u) mbar_wait_bounded(&ms.bar_stg[b], (stg_par >> b) & 1u, kWaitTimeoutNs / 4);
-    if (mma_pending) mbar_wait_bounded(&ms.bar_mma, mma_par, kWaitTimeoutNs / 4);
+    const uint64_t t_end = globaltimer_ns() + 200000ull;
+    while (globaltimer_ns() < t_end) {
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
