@@ -54,6 +54,7 @@ constexpr int kC = 64;
 constexpr int kThreads = 512;       // prep warps 0-7, chain warps 8-15
 constexpr int kGroup = 256;         // threads per group
 constexpr int kBarPrep = 1, kBarChain = 2;  // named hardware barriers of the groups
+constexpr int kPrepIssuer = 224;  // prep's MMA / copy issuer: warp 7, which the gate scan does not use
 constexpr uint32_t kCodeBytes = kD * kD / 2;
 constexpr uint32_t kScaleBytes = kD * kD / 16;
 
@@ -214,26 +215,25 @@ __device__ __forceinline__ int chunk_len(const Cursor& c) {
   return rest < kC ? (int)rest : kC;
 }
 
-// One thread: queue chunk c's k and q boxes into a stage.  Rows past the end
-// of the tensors arrive as zeros; rows past the end of the sequence are
-// masked by the consumers (beta = 0, rows not stored).
-__device__ __forceinline__ void issue_kq(const PrefillArgs& a, uint8_t* stage, uint64_t* bar, const Cursor& c,
-                                         const CUtensorMap* tq, const CUtensorMap* tk) {
+// Queue one of chunk c's four k and q boxes into a stage (part 0 also sets
+// the stage's byte count; the four parts are issued by four threads, since
+// one copy takes ~100 cycles to issue).  Rows past the end of the tensors
+// arrive as zeros; rows past the end of the sequence are masked by the
+// consumers (beta = 0, rows not stored).
+__device__ __forceinline__ void issue_kq_part(const PrefillArgs& a, uint8_t* stage, uint64_t* bar, const Cursor& c,
+                                              const CUtensorMap* tq, const CUtensorMap* tk, int part) {
   const int t0 = (int)(c.bos + c.chunk * kC);
   const int hk = c.h / a.group;
-  mbar_arrive_expect_tx(bar, kStageKQ);
-  tc::tma_load_3d(stage + kStK0, tk, 0, hk, t0, bar);
-  tc::tma_load_3d(stage + kStK1, tk, 64, hk, t0, bar);
-  tc::tma_load_3d(stage + kStQ0, tq, 0, hk, t0, bar);
-  tc::tma_load_3d(stage + kStQ1, tq, 64, hk, t0, bar);
+  if (part == 0) mbar_arrive_expect_tx(bar, kStageKQ);
+  const uint32_t off = part == 0 ? kStK0 : part == 1 ? kStK1 : part == 2 ? kStQ0 : kStQ1;
+  tc::tma_load_3d(stage + off, part < 2 ? tk : tq, 64 * (part & 1), hk, t0, bar);
 }
 
-__device__ __forceinline__ void issue_v(const PrefillArgs& a, uint8_t* vbuf, uint64_t* bar, const Cursor& c,
-                                        const CUtensorMap* tv) {
+__device__ __forceinline__ void issue_v_part(const PrefillArgs& a, uint8_t* vbuf, uint64_t* bar, const Cursor& c,
+                                             const CUtensorMap* tv, int part) {
   const int t0 = (int)(c.bos + c.chunk * kC);
-  mbar_arrive_expect_tx(bar, 2 * kBox);
-  tc::tma_load_3d(vbuf + kV0, tv, 0, c.h, t0, bar);
-  tc::tma_load_3d(vbuf + kV1, tv, 64, c.h, t0, bar);
+  if (part == 0) mbar_arrive_expect_tx(bar, 2 * kBox);
+  tc::tma_load_3d(vbuf + (part ? kV1 : kV0), tv, 64 * part, c.h, t0, bar);
 }
 
 // Threads 0..63: g and beta of token `r` of chunk c (0 past the chunk end).
@@ -324,19 +324,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       Hand& hd = hand[b];
       const bool last = (cur.chunk + 1) * kC >= cur.len;
 
-      // ---- P1 = [K; Q] K^T as soon as the stage has landed ----
-      if (!group_wait(&ms.bar_kq[b], (g >> 1) & 1, tid == 0, kBarPrep)) { failed = true; break; }
-      if (tid == 0) {
-        tc::fence_after_sync();
+      // ---- P1 = [K; Q] K^T as soon as the stage has landed (the issuer, while warps 0-1 scan the gates) ----
+      bool kq_ok = true;
+      if (tid == kPrepIssuer) {
+        kq_ok = mbar_wait_bounded(&ms.bar_kq[b], (g >> 1) & 1);
+        if (kq_ok) {
+          tc::fence_after_sync();
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint64_t dk = stage_kmajor(stage, kStK0, ks);
-          tc::mma_bf16_ss(T + kColKQ, dk, dk, id_kq, ks > 0);  // rows 64..127 of A are Q's box
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint64_t dk = stage_kmajor(stage, kStK0, ks);
+            tc::mma_bf16_ss(T + kColKQ, dk, dk, id_kq, ks > 0);  // rows 64..127 of A are Q's box
+          }
+          tc::commit(&ms.bar_p1);
         }
-        tc::commit(&ms.bar_p1);
       }
-      // ---- gates (the hand-over buffer is free once the chain has finished chunk g - 2) ----
-      if (g >= 2 && !group_wait(&ms.bar_hfree[b], ((g - 2) >> 1) & 1, tid == 0, kBarPrep)) { failed = true; break; }
+      // ---- gates ----
       const float gv = g_pre, bv = b_pre;
       if (tid < kC) {
         float s = gv;
@@ -351,6 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         load_gb(a, nx, tid, g_pre, b_pre);
       }
       group_sync(kBarPrep);
+      float h_de = 0.0f, h_qg = 0.0f, h_gC = 0.0f;
       if (tid < kC) {
         const float G = ms.gw[tid] + (tid >= 32 ? ms.gw[31] : 0.0f);
         const float Glast = ms.gw[63] + ms.gw[31];
@@ -359,14 +362,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         ms.bet[tid] = bv;
         ms.bg[tid] = bv * gm;
         ms.al[tid] = __expf(gv);
-        hd.de[tid] = __expf(Glast - G);
-        hd.qg[tid] = a.q_scale * gm;
-        if (tid == 0) hd.gC = __expf(Glast);
+        h_de = __expf(Glast - G);
+        h_qg = a.q_scale * gm;
+        h_gC = __expf(Glast);
       }
-      // ---- P1 done (and with it the previous chunk's P2: the v buffer and T diag(beta) are free) ----
-      if (!group_wait(&ms.bar_p1, g & 1, tid == 0, kBarPrep)) { failed = true; break; }
+      // ---- P1 done (and with it the previous chunk's P2: the v buffer and T diag(beta) are free), and
+      //      the hand-over buffer free (the chain has finished chunk g - 2): one wait for the group ----
+      {
+        bool ok = kq_ok;
+        if (tid == kPrepIssuer) {
+          if (ok && g >= 2) ok = mbar_wait_bounded(&ms.bar_hfree[b], ((g - 2) >> 1) & 1);
+          if (ok) ok = mbar_wait_bounded(&ms.bar_p1, g & 1);
+        }
+        if (group_or(kBarPrep, !ok)) { failed = true; break; }
+      }
       tc::fence_after_sync();
-      if (tid == 0) issue_v(a, vbuf, &ms.bar_v, cur, &tm_v);
+      if (tid < kC) {
+        hd.de[tid] = h_de;
+        hd.qg[tid] = h_qg;
+        if (tid == 0) hd.gC = h_gC;
+      }
+      if (tid == kPrepIssuer || tid == kPrepIssuer - 32)
+        issue_v_part(a, vbuf, &ms.bar_v, cur, &tm_v, tid == kPrepIssuer ? 0 : 1);
 
       // ---- A (strictly lower, for the solve) and P (lower incl. diagonal) ----
       // The decay exp(G_r - G_s) of this thread's columns s in [sb0, sb0 + 32)
@@ -513,8 +530,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc::fence_smem_to_async();
       // ---- v landed: P2 into U[b] (free since bar_hfree above); hand over to the chain ----
-      if (!group_wait(&ms.bar_v, g & 1, tid == 0, kBarPrep)) { failed = true; break; }
-      if (tid == 0) {
+      if (!group_wait(&ms.bar_v, g & 1, tid == kPrepIssuer, kBarPrep)) { failed = true; break; }
+      if (tid == kPrepIssuer) {
         tc::fence_after_sync();
         // P2: U^T = V^T T''^T  (A = V as MN-major, M = d_v, N = C, K = C)
 #pragma unroll
@@ -526,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (last) {
         // the chain transposes the final state through this group's scratch: wait for it
-        if (!group_wait(&ms.bar_seq, nseq & 1, tid == 0, kBarPrep)) { failed = true; break; }
+        if (!group_wait(&ms.bar_seq, nseq & 1, tid == kPrepIssuer, kBarPrep)) { failed = true; break; }
         ++nseq;
       }
       ++g;
@@ -546,7 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     Cursor ahead = cur;  // next chunk whose k/q to load
     for (int b = 0; b < 2; ++b) {
       if (ahead.item < a.nitems) {
-        if (ctid == 0) issue_kq(a, smem + kOffKQ + b * kStageKQ, &ms.bar_kq[b], ahead, &tm_q, &tm_k);
+        if (lane == 0 && warp < 12) issue_kq_part(a, smem + kOffKQ + b * kStageKQ, &ms.bar_kq[b], ahead, &tm_q, &tm_k, warp - 8);
         cursor_next(a, ahead, false);
       }
     }
@@ -718,7 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       s_zero = false;
       // The stage is free: queue the chunk after next into it.
       if (ahead.item < a.nitems) {
-        if (ctid == 0) issue_kq(a, stage, &ms.bar_kq[b], ahead, &tm_q, &tm_k);
+        if (lane == 0 && warp >= 12) issue_kq_part(a, stage, &ms.bar_kq[b], ahead, &tm_q, &tm_k, warp - 12);
         cursor_next(a, ahead, false);
       }
 
