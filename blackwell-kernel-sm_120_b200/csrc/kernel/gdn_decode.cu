@@ -158,9 +158,9 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
   }
 }
 
-__device__ __forceinline__ uint16_t f2bf_bits(float f) {
-  const __nv_bfloat16 b = __float2bfloat16_rn(f);
-  return *reinterpret_cast<const uint16_t*>(&b);
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&p);
 }
 
 template <int kMode, bool kDebug>
@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float o1 = __shfl_down_sync(0xffffffffu, o, 1);
       if ((j & 1) == 0)
         reinterpret_cast<uint32_t*>(a.out + ((int64_t)m.b * a.HV + m.h) * kD)[j >> 1] =
-            (uint32_t)f2bf_bits(o) | ((uint32_t)f2bf_bits(o1) << 16);
+            pack_bf16x2(o, o1);  // one paired conversion (faster than two single ones)
       const float wc = wj * m.inv_c;
       const float hi = __uint_as_float(__float_as_uint(wc) & 0xFFFFE000u);
       uint8_t* bw = sm.bw[n & 1];
