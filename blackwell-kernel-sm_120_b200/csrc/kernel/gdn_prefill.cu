@@ -764,13 +764,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::ld_32x32b_x16(T + lane_base + kColO2 + col, v2);
         if (!s0) tc::ld_32x32b_x16(T + lane_base + kColO1 + col, v1);
         tc::ld_wait();
-        __nv_bfloat16* orow = a.out + (t0 + col) * row_stride + (int64_t)h * kD + lrow;
+        // Rows r, r + 1 per step: an even lane j stores (j, j + 1) of row r, an odd lane (j - 1, j) of
+        // row r + 1, after one shuffle with its neighbour: 4-byte stores, one paired conversion.
+        const bool odd = lane & 1;
+        uint32_t* orow = reinterpret_cast<uint32_t*>(a.out + (t0 + col + (odd ? 1 : 0)) * row_stride +
+                                                     (int64_t)h * kD + (lrow & ~1));
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
+        for (int c = 0; c < 16; c += 2) {
           const int r = col + c;
-          const float o = s0 ? v2[c] : fmaf(hd.qg[r], v1[c], v2[c]);
-          if (r < len) *orow = __float2bfloat16_rn(o);
-          orow += row_stride;
+          const float o0 = s0 ? v2[c] : fmaf(hd.qg[r], v1[c], v2[c]);
+          const float o1 = s0 ? v2[c + 1] : fmaf(hd.qg[r + 1], v1[c + 1], v2[c + 1]);
+          const float x = __shfl_xor_sync(0xffffffffu, odd ? o0 : o1, 1);
+          const uint32_t pk = odd ? pack_bf16(x, o1) : pack_bf16(o0, x);
+          if (r + (odd ? 1 : 0) < len) *orow = pk;
+          orow += row_stride;  // two rows of row_stride / 2 words
         }
       }
       tc::fence_before_sync();
