@@ -142,7 +142,17 @@ struct DecodeArgs {
   float q_scale, gden;
   float* debug_y;
   uint32_t* status;
+  // fused prologue (A_log == nullptr: g and beta are read)
+  const float* A_log;
+  const float* dt_bias;
+  const __nv_bfloat16* gate_a;
+  const __nv_bfloat16* gate_b;
+  int64_t gate_stride;
+  int32_t qk_l2norm;
 };
+
+// softplus(x) = log(1 + exp(x)), the identity above 20 (torch.nn.functional.softplus, beta 1).
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
 // Bounded wait that also gives up when another role has aborted.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
@@ -235,9 +245,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         r.slot = __ldg(a.slot_idx + r.b);
         if (r.slot >= 0 && r.slot < a.num_slots) {
           r.pt = (int64_t)r.slot * a.HV + r.h;
-          const int64_t gi = (int64_t)r.b * a.HV + r.h;
-          r.c = expf(__ldg(a.g + gi)) * __ldg(a.pool_gs + r.pt);
-          r.beta = __ldg(a.beta + gi);
+          float gv, bv;
+          if (a.A_log) {  // fused gating: g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)
+            const int64_t ai = (int64_t)r.b * a.gate_stride + r.h;
+            const float av = __bfloat162float(a.gate_a[ai]), bb = __bfloat162float(a.gate_b[ai]);
+            gv = -expf(__ldg(a.A_log + r.h)) * softplus_f(av + __ldg(a.dt_bias + r.h));
+            bv = 1.0f / (1.0f + expf(-bb));
+          } else {
+            const int64_t gi = (int64_t)r.b * a.HV + r.h;
+            gv = __ldg(a.g + gi);
+            bv = __ldg(a.beta + gi);
+          }
+          r.c = expf(gv) * __ldg(a.pool_gs + r.pt);
+          r.beta = bv;
         }
       }
       return r;
@@ -324,12 +344,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           sfw[t * 128 + m0 * 4 + m1] = scw[(32 * m1 + m0) * 2 + t];
         }
         float kq = 0.0f;
+        // optional unit-L2 scaling of k and q (fp32), x / sqrt(sum x^2 + 1e-6)
+        float sk = 1.0f, sq = 1.0f;
+        if (a.qk_l2norm) {
+          float nk = 0.0f, nq = 0.0f;
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const int i2 = lane + 32 * r;
+            const float2 k2 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(st.k)[i2]);
+            const float2 q2 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(st.q)[i2]);
+            nk = fmaf(k2.x, k2.x, fmaf(k2.y, k2.y, nk));
+            nq = fmaf(q2.x, q2.x, fmaf(q2.y, q2.y, nq));
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            nk += __shfl_xor_sync(0xffffffffu, nk, o);
+            nq += __shfl_xor_sync(0xffffffffu, nq, o);
+          }
+          sk = 1.0f / sqrtf(nk + 1e-6f);
+          sq = 1.0f / sqrtf(nq + 1e-6f);
+        }
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
           const int i2 = lane + 32 * r;  // pair (2 i2, 2 i2 + 1)
           const __nv_bfloat162 k2 = reinterpret_cast<const __nv_bfloat162*>(st.k)[i2];
           const __nv_bfloat162 q2 = reinterpret_cast<const __nv_bfloat162*>(st.q)[i2];
-          const float4 f = make_float4(__low2float(k2), __high2float(k2), __low2float(q2), __high2float(q2));
+          const float4 f = make_float4(__low2float(k2) * sk, __high2float(k2) * sk, __low2float(q2) * sq,
+                                       __high2float(q2) * sq);
           st.kq4[i2] = f;
           kq = fmaf(f.x, f.z, fmaf(f.y, f.w, kq));
           *reinterpret_cast<float2*>(st.ak + kf32(2 * i2, 0, 256)) = make_float2(f.x, f.x);
@@ -584,8 +625,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
   if (!p) return GDN_ERR_ARGS;
-  if (!p->q || !p->k || !p->v || !p->g || !p->beta || !p->slot_idx || !p->pool_codes || !p->pool_scales ||
-      !p->pool_gscale || !p->out)
+  if (!p->q || !p->k || !p->v || (!p->A_log && (!p->g || !p->beta)) || !p->slot_idx || !p->pool_codes ||
+      !p->pool_scales || !p->pool_gscale || !p->out)
     return GDN_ERR_ARGS;
   if (p->batch < 0 || p->num_k_heads <= 0 || p->num_v_heads <= 0 || p->num_slots < 0) return GDN_ERR_ARGS;
   if (p->num_v_heads % p->num_k_heads) return GDN_ERR_ARGS;
@@ -626,6 +667,13 @@ extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
   a.debug_y = p->debug_y;
   a.status = device_status_ptr();
   if (!a.status) return GDN_ERR_CUDA;
+  a.A_log = p->A_log;
+  a.dt_bias = p->dt_bias;
+  a.gate_a = p->gate_a;
+  a.gate_b = p->gate_b;
+  a.gate_stride = p->gate_stride ? p->gate_stride : p->num_v_heads;
+  a.qk_l2norm = p->qk_l2norm;
+  if (a.A_log && (!a.dt_bias || !a.gate_a || !a.gate_b || a.gate_stride < p->num_v_heads)) return GDN_ERR_ARGS;
 
   CUtensorMap tm;
   {

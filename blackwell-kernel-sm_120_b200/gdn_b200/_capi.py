@@ -62,6 +62,8 @@ class DecodeParams(ctypes.Structure):
         ("out", _p),
         ("q_scale", _f32), ("scale_mode", _i32), ("gscale_den", _f32),
         ("debug_y", _p),
+        ("A_log", _p), ("dt_bias", _p), ("gate_a", _p), ("gate_b", _p), ("gate_stride", _i64),
+        ("qk_l2norm", _i32),
     ]
 
 

@@ -125,19 +125,42 @@ def legacy_set_rounding(variant: int) -> int:
 
 # ---- decode ------------------------------------------------------------------------
 
-def decode(q, k, v, g, beta, slot_idx, pool, out=None, q_scale: float = 0.0, debug_y=None):
+def decode(q, k, v, g, beta, slot_idx, pool, out=None, q_scale: float = 0.0, debug_y=None, *, A_log=None,
+           dt_bias=None, gate_a=None, gate_b=None, qk_l2norm: bool = False):
     """One fused gated-delta-rule decode step over the NVFP4 pool `pool`
     (gdn_b200.pool.NVFP4StatePool).  q, k: [B, HK, D] bf16; v: [B, HV, D] bf16;
-    g, beta: [B, HV] fp32; slot_idx: [B] int32.  Returns out [B, HV, D] bf16."""
+    g, beta: [B, HV] fp32; slot_idx: [B] int32.  Returns out [B, HV, D] bf16.
+
+    Fused prologue (vLLM's gating and q/k normalisation): with A_log ([HV] fp32),
+    dt_bias ([HV] fp32) and the gate projections gate_a, gate_b ([B, HV] bf16),
+    g = -exp(A_log) softplus(gate_a + dt_bias) and beta = sigmoid(gate_b) are
+    computed in the kernel (g and beta may then be None); qk_l2norm scales q and
+    k to unit L2 norm per head in the kernel."""
     B, HK, D = q.shape
     HV = v.shape[1]
     for t, name in ((q, "q"), (k, "k"), (v, "v")):
         if t.dtype != torch.bfloat16 or not t.is_cuda or t.stride(-1) != 1 or t.stride(-2) != D:
             raise ValueError(f"{name} must be CUDA bf16 with contiguous heads")
-    _need(g, torch.float32, "g")
-    _need(beta, torch.float32, "beta")
+    fused = A_log is not None
+    if fused:
+        if dt_bias is None:
+            raise ValueError("dt_bias is required with A_log")
+        _need(A_log, torch.float32, "A_log")
+        _need(dt_bias, torch.float32, "dt_bias")
+        for t, name in ((gate_a, "gate_a"), (gate_b, "gate_b")):
+            if t is None or t.dtype != torch.bfloat16 or not t.is_cuda or t.shape != (B, HV) or t.stride(-1) != 1:
+                raise ValueError(f"{name} must be CUDA bf16 [B, HV] with contiguous heads")
+        if gate_a.stride(0) != gate_b.stride(0) or A_log.shape != (HV,) or dt_bias.shape != (HV,):
+            raise ValueError("gate shapes or strides do not match")
+    else:
+        if g is None or beta is None:
+            raise ValueError("g and beta are required unless the gate inputs (A_log, ...) are given")
+        _need(g, torch.float32, "g")
+        _need(beta, torch.float32, "beta")
+        if g.shape != (B, HV) or beta.shape != (B, HV):
+            raise ValueError("shape mismatch")
     _need(slot_idx, torch.int32, "slot_idx")
-    if k.shape != (B, HK, D) or v.shape != (B, HV, D) or g.shape != (B, HV) or beta.shape != (B, HV):
+    if k.shape != (B, HK, D) or v.shape != (B, HV, D):
         raise ValueError("shape mismatch")
     if pool.num_v_heads != HV or pool.head_dim != D:
         raise ValueError("pool does not match the head layout")
@@ -148,13 +171,17 @@ def decode(q, k, v, g, beta, slot_idx, pool, out=None, q_scale: float = 0.0, deb
     p.num_slots = pool.num_slots
     p.q, p.k, p.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
     p.q_stride, p.k_stride, p.v_stride = q.stride(0), k.stride(0), v.stride(0)
-    p.g, p.beta, p.slot_idx = g.data_ptr(), beta.data_ptr(), slot_idx.data_ptr()
+    p.g, p.beta, p.slot_idx = _ptr(g), _ptr(beta), slot_idx.data_ptr()
     p.pool_codes, p.pool_scales, p.pool_gscale = pool.codes.data_ptr(), pool.scales.data_ptr(), pool.gscale.data_ptr()
     p.out = out.data_ptr()
     p.q_scale = q_scale
     p.scale_mode = pool.scale_mode
     p.gscale_den = pool.gscale_den
     p.debug_y = _ptr(debug_y)
+    if fused:
+        p.A_log, p.dt_bias = A_log.data_ptr(), dt_bias.data_ptr()
+        p.gate_a, p.gate_b, p.gate_stride = gate_a.data_ptr(), gate_b.data_ptr(), gate_a.stride(0)
+    p.qk_l2norm = 1 if qk_l2norm else 0
     check("gdn_decode", lib.gdn_decode(ctypes.byref(p), _stream(q)))
     return out
 

@@ -93,17 +93,16 @@ def fused_sigmoid_gating_delta_rule_update(A_log, a, b, dt_bias, q, k, v, initia
         raise NotImplementedError("speculative decoding is outside this kernel's scope")
     qs, ks, vs = q.reshape(-1, *q.shape[-2:]), k.reshape(-1, *k.shape[-2:]), v.reshape(-1, *v.shape[-2:])
     B = qs.shape[0]
-    if use_qk_l2norm_in_kernel:
-        qs = F.normalize(qs.float(), dim=-1)
-        ks = F.normalize(ks.float(), dim=-1)
     qs, ks, vs = (t.to(torch.bfloat16).contiguous() for t in (qs, ks, vs))
-    g, beta = gating(A_log, a.reshape(B, -1), b.reshape(B, -1), dt_bias)
     idx = ssm_state_indices.to(torch.int64) if ssm_state_indices is not None else torch.arange(B, device=q.device)
     valid = idx >= 0
     dense = initial_state[idx.clamp(min=0)]
     pool = _to_pool(dense, scale_mode)
     slot = torch.where(valid, torch.arange(B, device=q.device), torch.full_like(idx, -1)).to(torch.int32)
-    o = ops.decode(qs, ks, vs, g, beta, slot, pool)
+    # gating and the q/k normalisation run inside the decode kernel
+    o = ops.decode(qs, ks, vs, None, None, slot, pool, A_log=A_log.float().contiguous(),
+                   dt_bias=dt_bias.float().contiguous(), gate_a=a.reshape(B, -1).to(torch.bfloat16),
+                   gate_b=b.reshape(B, -1).to(torch.bfloat16), qk_l2norm=use_qk_l2norm_in_kernel)
     new = _from_pool(pool, initial_state.dtype)
     if inplace_final_state:
         initial_state[idx[valid]] = new[valid]

@@ -158,6 +158,18 @@ typedef struct gdn_decode_params {
   int32_t scale_mode;     /* GDN_SCALE_* */
   float gscale_den;       /* <= 0 selects 6*saturation */
   float* debug_y;         /* optional [B, HV, D, D]: the fp32 quantiser inputs */
+  /* Optional fused prologue (the gating and q/k normalisation vLLM runs before
+   * the recurrence; all NULL / 0 to skip).  With A_log set, g and beta are
+   * computed in the kernel from the gate projections and the g / beta fields
+   * are not read:
+   *   g = -exp(A_log[h]) * softplus(gate_a[b, h] + dt_bias[h]),  beta = sigmoid(gate_b[b, h])
+   * (softplus with threshold 20, as torch.nn.functional.softplus). */
+  const float* A_log;       /* [HV] */
+  const float* dt_bias;     /* [HV] */
+  const gdn_bf16_t* gate_a; /* [B, HV], sequence stride gate_stride */
+  const gdn_bf16_t* gate_b; /* [B, HV], sequence stride gate_stride */
+  int64_t gate_stride;      /* elements between sequences; 0 = HV */
+  int32_t qk_l2norm;        /* != 0: q and k scaled to unit L2 norm per head, x / sqrt(sum x^2 + 1e-6), in fp32 */
 } gdn_decode_params;
 
 GDN_API int gdn_decode(const gdn_decode_params* params, cudaStream_t stream);

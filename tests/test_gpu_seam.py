@@ -90,13 +90,19 @@ def test_seam_decode_in_place(cuda):
         inplace_final_state=True, ssm_state_indices=idx, use_qk_l2norm_in_kernel=False)
     torch.cuda.synchronize()
     assert st is ssm and o.shape == (1, B, HV, D)
-    # same kernel through the C ABI on the same NVFP4 tiles
-    g, beta = vllm_seam.gating(A_log, a, b, dt_bias)
+    # same kernel (gating fused in, from the bf16 gate projections) through the C ABI on the same NVFP4 tiles
     pool = NVFP4StatePool.zeros(B, HV, D, "cuda")
     pool.load_fp32(before[idx.long().clamp(min=0)].transpose(-1, -2).contiguous())
     slot = torch.tensor([0, -1, 2, 3, 4, 5], dtype=torch.int32, device="cuda")
-    o_ref = ops.decode(x["q"][0], x["k"][0], x["v"][0], g, beta, slot, pool)
+    o_ref = ops.decode(x["q"][0], x["k"][0], x["v"][0], None, None, slot, pool, A_log=A_log, dt_bias=dt_bias,
+                       gate_a=a.to(torch.bfloat16), gate_b=b.to(torch.bfloat16))
     assert torch.equal(o[0], o_ref)
+    # and the torch gating of the same bf16 projections agrees to the last bits of exp / log1p
+    g, beta = vllm_seam.gating(A_log, a.to(torch.bfloat16), b.to(torch.bfloat16), dt_bias)
+    pool2 = NVFP4StatePool.zeros(B, HV, D, "cuda")
+    pool2.load_fp32(before[idx.long().clamp(min=0)].transpose(-1, -2).contiguous())
+    o_host = ops.decode(x["q"][0], x["k"][0], x["v"][0], g, beta, slot, pool2)
+    assert float((o_host.float() - o_ref.float()).abs().max()) <= 1e-2 * float(o_ref.float().abs().max())
     new = pool.dequantize().transpose(-1, -2)
     for i, s in enumerate(idx.tolist()):
         if s >= 0:
