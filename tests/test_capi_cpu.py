@@ -78,3 +78,31 @@ def test_error_strings_and_version():
     from gdn_b200 import _capi
     assert _capi.lib.gdn_b200_error_string(1).decode().startswith("invalid argument")
     assert "sm_100a" in _capi.version()
+
+
+@pytest.mark.parametrize("struct_name,py_name", [("gdn_decode_params", "DecodeParams"),
+                                                 ("gdn_prefill_params", "PrefillParams")])
+def test_ctypes_mirrors_match_the_c_layout(tmp_path, struct_name, py_name):
+    """The ctypes parameter blocks have the C header's size and field offsets
+    (a C program built here with gcc prints them)."""
+    import shutil
+    import subprocess
+    from gdn_b200 import _capi
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    py = getattr(_capi, py_name)
+    fields = [f[0] for f in py._fields_]
+    lines = [f'printf("%zu\\n", sizeof({struct_name}));']
+    lines += [f'printf("%zu\\n", offsetof({struct_name}, {f}));' for f in fields]
+    src = tmp_path / "layout.c"
+    src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include <stdint.h>\n"
+                   "typedef struct CUstream_st* cudaStream_t;\n"
+                   f'#include "{HEADER}"\n'
+                   "int main(void) {\n  " + "\n  ".join(lines) + "\n  return 0;\n}\n")
+    exe = tmp_path / "layout"
+    cuda_inc = "/usr/local/cuda/include"
+    r = subprocess.run(["gcc", "-std=c11", f"-I{cuda_inc}", str(src), "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    assert out[0] == ctypes.sizeof(py)
+    assert out[1:] == [getattr(py, f).offset for f in fields]
