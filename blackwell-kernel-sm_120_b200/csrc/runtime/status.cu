@@ -47,7 +47,34 @@ int sm_count() {
   return g_sm_count[dev];
 }
 
+// Exercises the bounded mbarrier wait every kernel uses (common.cuh) on both
+// of its exits: a phase that completes (one arrival) and a phase that nothing
+// completes, which must give up after timeout_ns and record the timeout bit.
+// result = {first wait returned true, second returned true, microseconds the
+// second waited}.
+__global__ void wait_selftest_kernel(uint64_t timeout_ns, int32_t* result) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  mbar_arrive(&bar);  // completes phase 0
+  const bool done = mbar_wait_bounded(&bar, 0, timeout_ns);
+  const uint64_t t0 = globaltimer_ns();
+  const bool stuck = mbar_wait_bounded(&bar, 1, timeout_ns);  // phase 1 gets no arrival
+  const uint64_t waited = globaltimer_ns() - t0;
+  if (!stuck) atomicOr(&g_device_status, kStatusWaitTimeout);
+  result[0] = done ? 1 : 0;
+  result[1] = stuck ? 1 : 0;
+  result[2] = (int32_t)(waited / 1000u);
+}
+
 }  // namespace gdn
+
+extern "C" int gdn_b200_selftest_wait(uint32_t timeout_us, int32_t* result, cudaStream_t stream) {
+  if (!result || timeout_us == 0 || timeout_us > 2000000u) return GDN_ERR_ARGS;
+  gdn::wait_selftest_kernel<<<1, 32, 0, stream>>>((uint64_t)timeout_us * 1000u, result);
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
 
 extern "C" int gdn_b200_device_status(uint32_t* status_out, int clear, cudaStream_t stream) {
   if (!status_out) return GDN_ERR_ARGS;

@@ -40,6 +40,7 @@ EXPORTED_SYMBOLS = (
     "gdn_pool_gather",
     "gdn_pool_scatter",
     "gdn_b200_device_status",
+    "gdn_b200_selftest_wait",
     "gdn_b200_error_string",
     "gdn_b200_version",
 )
@@ -108,6 +109,7 @@ def _load() -> ctypes.CDLL:
         "gdn_pool_gather": (ctypes.c_int, [_p, _p, _p, _i64, _i32, _i32, _p, _i32, _p, _p, _p, _p]),
         "gdn_pool_scatter": (ctypes.c_int, [_p, _p, _p, _i64, _i32, _i32, _p, _i32, _p, _p, _p, _p]),
         "gdn_b200_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, _p]),
+        "gdn_b200_selftest_wait": (ctypes.c_int, [ctypes.c_uint32, _p, _p]),
         "gdn_b200_error_string": (ctypes.c_char_p, [ctypes.c_int]),
         "gdn_b200_version": (ctypes.c_char_p, []),
     }

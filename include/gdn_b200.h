@@ -235,6 +235,14 @@ GDN_API int gdn_pool_scatter(const uint8_t* dense_codes, const uint8_t* dense_sc
  * device after synchronising `stream`.  This call blocks the host. */
 GDN_API int gdn_b200_device_status(uint32_t* status_out, int clear, cudaStream_t stream);
 
+/* Self-test of the bounded wait behind GDN_STATUS_WAIT_TIMEOUT (no counterpart
+ * in the reference, whose waits are host-side).  One thread on the device waits
+ * on an mbarrier phase that completes, then on one that nothing completes;
+ * the second wait must give up after timeout_us (1 .. 2,000,000) and set
+ * GDN_STATUS_WAIT_TIMEOUT.  result: device int32[3] = {first wait succeeded,
+ * second wait succeeded, microseconds the second waited}.  Stream-ordered. */
+GDN_API int gdn_b200_selftest_wait(uint32_t timeout_us, int32_t* result, cudaStream_t stream);
+
 GDN_API const char* gdn_b200_error_string(int code);
 GDN_API const char* gdn_b200_version(void);
 
