@@ -13,14 +13,17 @@ Timing: W untimed warm-up steps, then exactly K steps bracketed by a barrier
 and torch.cuda.synchronize(), measured with CUDA events on the launching
 stream; the whole-job time is the max over ranks.  Inputs rotate over 6 pools
 and 6 input sets (453 MB, larger than the 126 MB L2), so every step reads its
-state from HBM.  Per-launch kernel durations come from events around each
-launch and give the roofline figure: achieved = 614,916 algorithmic bytes per
-token (NVFP4 state read + write, global scales, bf16 q/k/v/o, g/beta, slot
-index) x 256 tokens / mean launch duration.
+state from HBM.  There is one kernel launch per step, so the mean launch
+duration is the timed region over K, and it gives the roofline figure:
+achieved = 614,916 algorithmic bytes per token (NVFP4 state read + write,
+global scales, bf16 q/k/v/o, g/beta, slot index) x 256 tokens / mean launch
+duration.
 
 The e2e figure is the same metric through the public API with host buffers:
-per step, pinned-host -> device copies of that step's q, k, v, g, beta and slot
-indices, the decode call, and a device -> pinned-host copy of its outputs.
+per step, one pinned-host -> device copy of that step's inputs (the fused qkv
+projection rows, of which q, k and v are strided views, then g, beta and the
+slot indices), the decode call, and a device -> pinned-host copy of its
+outputs.
 
 rank 0 at N = 1 also times the CPU path (the reference's NVFP4 host codec from
 oracle/_ref around a C restatement of the GDN step, all host threads) on a
@@ -267,8 +270,10 @@ def run_ours(args, dist, rank, world, local) -> dict | None:
     if ops.device_status(clear=True):
         raise RuntimeError("device status set during warm-up")
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    # One kernel launch per step, back to back on one stream: each launch's
+    # set-up overlaps the previous one's tail (programmatic dependent launch),
+    # so the mean launch duration is the timed region over K.  Event pairs
+    # around every launch would serialise the launches and add their own cost.
     t_begin = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     _barrier(dist)
@@ -276,33 +281,47 @@ def run_ours(args, dist, rank, world, local) -> dict | None:
     with ClockSampler(local) as clocks:
         t_begin.record(stream)
         for i in range(args.steps):
-            starts[i].record(stream)
             step(args.warmup + i)
-            ends[i].record(stream)
         t_end.record(stream)
         torch.cuda.synchronize()
     _barrier(dist)
-    total_ms = t_begin.elapsed_time(t_end)
-    launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = _max_over_ranks(dist, total_ms)
-    mean_launch_ms = _max_over_ranks(dist, sum(launch_ms) / len(launch_ms))
+    total_ms = _max_over_ranks(dist, t_begin.elapsed_time(t_end))
+    mean_launch_ms = total_ms / args.steps
     if ops.device_status(clear=True):
         raise RuntimeError("device status set during the timed region")
 
-    # e2e: through the public API with pinned host buffers.  Every step copies
-    # its own inputs host -> device and its outputs device -> host; one copy
-    # stream moves step i+1's inputs and another step i-1's outputs while step
-    # i computes (double buffers).
-    host_in = []
+    # e2e: through the public API with pinned host buffers.  Each step's inputs
+    # travel in one host -> device copy, laid out as a serving engine holds
+    # them: the fused qkv projection rows [B, (2 HK + HV) D] bf16 (q, k and v
+    # are strided views of it), then g and beta [B, HV] fp32 and the slot
+    # index.  The outputs come back in one device -> host copy.  One copy
+    # stream moves step i+1's inputs and another step i's outputs while the
+    # compute stream runs step i (double buffers).
+    width = (2 * HK + HV) * D
+    qkv_bytes = B * width * 2
+    gb_bytes = B * HV * 4
+    pack_bytes = qkv_bytes + 2 * gb_bytes + B * 4
+
+    def views(buf):
+        qkv = buf[:qkv_bytes].view(torch.bfloat16).view(B, 2 * HK + HV, D)
+        g = buf[qkv_bytes:qkv_bytes + gb_bytes].view(torch.float32).view(B, HV)
+        be = buf[qkv_bytes + gb_bytes:qkv_bytes + 2 * gb_bytes].view(torch.float32).view(B, HV)
+        sl = buf[qkv_bytes + 2 * gb_bytes:].view(torch.int32)
+        return {"q": qkv[:, :HK], "k": qkv[:, HK:2 * HK], "v": qkv[:, 2 * HK:], "g": g, "beta": be}, sl
+
+    host_pack = []
     for i in range(N_POOLS):
-        x = inputs[i]
-        host_in.append({k2: t.cpu().pin_memory() for k2, t in x.items()})
-    host_slot = slot.cpu().pin_memory()
-    dev_in = [{k2: torch.empty_like(t) for k2, t in inputs[0].items()} for _ in range(2)]
-    dev_slot = [torch.empty_like(slot) for _ in range(2)]
+        hb = torch.empty(pack_bytes, dtype=torch.uint8).pin_memory()
+        hv, hs = views(hb)
+        for k2, t in inputs[i].items():
+            hv[k2].copy_(t.cpu())
+        hs.copy_(slot.cpu())
+        host_pack.append(hb)
+    dev_pack = [torch.empty(pack_bytes, dtype=torch.uint8, device=dev) for _ in range(2)]
+    dev_views = [views(buf) for buf in dev_pack]
     dev_out = [torch.empty((B, HV, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     host_out = [torch.empty((B, HV, D), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    h2d = sum(t.numel() * t.element_size() for t in host_in[0].values()) + host_slot.numel() * 4
+    h2d = pack_bytes
     d2h = host_out[0].numel() * 2
     e2e_steps = max(1, min(args.steps, 200))
     copy_stream = torch.cuda.Stream(dev)   # host -> device, one step ahead
@@ -316,10 +335,15 @@ def run_ours(args, dist, rank, world, local) -> dict | None:
         b = i % 2
         with torch.cuda.stream(copy_stream):
             copy_stream.wait_event(consumed[b])
-            for k2 in dev_in[b]:
-                dev_in[b][k2].copy_(host_in[i % N_POOLS][k2], non_blocking=True)
-            dev_slot[b].copy_(host_slot, non_blocking=True)
+            dev_pack[b].copy_(host_pack[i % N_POOLS], non_blocking=True)
             loaded[b].record(copy_stream)
+
+    def drain(i):
+        b = i % 2
+        with torch.cuda.stream(back_stream):
+            back_stream.wait_event(computed[b])
+            host_out[b].copy_(dev_out[b], non_blocking=True)
+            drained[b].record(back_stream)
 
     def e2e_run(n):
         for b in range(2):
@@ -328,18 +352,16 @@ def run_ours(args, dist, rank, world, local) -> dict | None:
         load(0)
         for i in range(n):
             b = i % 2
-            if i + 1 < n:
-                load(i + 1)
             stream.wait_event(loaded[b])
             stream.wait_event(drained[b])  # the output buffer's previous copy-out is done
-            x = dev_in[b]
-            ops.decode(x["q"], x["k"], x["v"], x["g"], x["beta"], dev_slot[b], pools[i % N_POOLS], out=dev_out[b])
+            x, sl = dev_views[b]
+            ops.decode(x["q"], x["k"], x["v"], x["g"], x["beta"], sl, pools[i % N_POOLS], out=dev_out[b])
             consumed[b].record(stream)
             computed[b].record(stream)
-            with torch.cuda.stream(back_stream):
-                back_stream.wait_event(computed[b])
-                host_out[b].copy_(dev_out[b], non_blocking=True)
-                drained[b].record(back_stream)
+            if i + 1 < n:
+                load(i + 1)
+            drain(i)
+        stream.wait_stream(copy_stream)
         stream.wait_stream(back_stream)
 
     e2e_run(3)

@@ -222,6 +222,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t T = sm.tmem_base;
+  // Launched as a programmatic dependent: the set-up above (shared and tensor
+  // memory only) overlaps the previous kernel's tail; nothing in global memory
+  // is read or written before every grid this one depends on has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // The next launch in the stream may start its set-up as SMs free up.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == kProdWarp) {
     // =================================== producer ===================================
@@ -708,6 +714,19 @@ extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
       return GDN_ERR_CUDA;
     attr_set[mi][dev] = true;
   }
-  kern<<<grid, kThreads, smem, stream>>>(a, tm);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, a, tm) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return GDN_ERR_LAUNCH;
+  }
   return launch_status();
 }
