@@ -232,49 +232,66 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kProdWarp) {
     // =================================== producer ===================================
     // Lane l loads the scalars of tile t0 + l * gridDim.x for a batch of 32
-    // tiles at a time (the next batch's loads are in flight while this one is
-    // queued), so the dependent slot -> global-scale loads cost one latency
-    // per 32 tiles; lane 0 queues the copies in tile order.
+    // tiles at a time; lane 0 queues the copies in tile order.  The next
+    // batch's independent loads (slot, g and beta or the gate inputs) are in
+    // flight while this batch is queued, and its dependent global-scale load
+    // follows the queueing, so the first copy waits for one batch only.
     struct Scal {
       int64_t pt;
       int32_t b, h, slot;
       float c, beta;
       int32_t live;  // tile index < ntiles
     };
-    auto load_batch = [&](int64_t tb0) -> Scal {
-      Scal r{0, 0, 0, -1, 0.0f, 0.0f, 0};
-      const int64_t t = tb0 + (int64_t)lane * gridDim.x;
+    struct Raw {
+      int32_t b, h, slot, live;
+      float x0, x1, x2, x3;  // g, beta; or gate a, gate b, A_log, dt_bias
+    };
+    auto issue_batch = [&](int64_t tb) -> Raw {
+      Raw r{0, 0, -1, 0, 0.0f, 0.0f, 0.0f, 0.0f};
+      const int64_t t = tb + (int64_t)lane * gridDim.x;
       if (t < a.ntiles) {
         r.live = 1;
         r.b = (int32_t)(t / a.HV);
         r.h = (int32_t)(t - (int64_t)r.b * a.HV);
         r.slot = __ldg(a.slot_idx + r.b);
-        if (r.slot >= 0 && r.slot < a.num_slots) {
-          r.pt = (int64_t)r.slot * a.HV + r.h;
-          float gv, bv;
-          if (a.A_log) {  // fused gating: g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)
-            const int64_t ai = (int64_t)r.b * a.gate_stride + r.h;
-            const float av = __bfloat162float(a.gate_a[ai]), bb = __bfloat162float(a.gate_b[ai]);
-            gv = -expf(__ldg(a.A_log + r.h)) * softplus_f(av + __ldg(a.dt_bias + r.h));
-            bv = 1.0f / (1.0f + expf(-bb));
-          } else {
-            const int64_t gi = (int64_t)r.b * a.HV + r.h;
-            gv = __ldg(a.g + gi);
-            bv = __ldg(a.beta + gi);
-          }
-          r.c = expf(gv) * __ldg(a.pool_gs + r.pt);
-          r.beta = bv;
+        if (a.A_log) {
+          const int64_t ai = (int64_t)r.b * a.gate_stride + r.h;
+          r.x0 = __bfloat162float(a.gate_a[ai]);
+          r.x1 = __bfloat162float(a.gate_b[ai]);
+          r.x2 = __ldg(a.A_log + r.h);
+          r.x3 = __ldg(a.dt_bias + r.h);
+        } else {
+          const int64_t gi = (int64_t)r.b * a.HV + r.h;
+          r.x0 = __ldg(a.g + gi);
+          r.x1 = __ldg(a.beta + gi);
         }
       }
       return r;
     };
+    auto finish_batch = [&](const Raw& r) -> Scal {
+      Scal q{0, r.b, r.h, r.slot, 0.0f, 0.0f, r.live};
+      if (r.live && r.slot >= 0 && r.slot < a.num_slots) {
+        q.pt = (int64_t)r.slot * a.HV + r.h;
+        float gv, bv;
+        if (a.A_log) {  // fused gating: g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)
+          gv = -expf(r.x2) * softplus_f(r.x0 + r.x3);
+          bv = 1.0f / (1.0f + expf(-r.x1));
+        } else {
+          gv = r.x0;
+          bv = r.x1;
+        }
+        q.c = expf(gv) * __ldg(a.pool_gs + q.pt);
+        q.beta = bv;
+      }
+      return q;
+    };
     int64_t tb0 = blockIdx.x;
     const int64_t batch_step = 32ll * gridDim.x;
-    Scal cur = load_batch(tb0);
+    Scal cur = finish_batch(issue_batch(tb0));
     int n = 0;
     bool done = false, ok = true;
     while (!done && ok) {
-      const Scal nxt = load_batch(tb0 + batch_step);
+      const Raw nxt = issue_batch(tb0 + batch_step);
       for (int l = 0; l < 32; ++l) {
         const int live = __shfl_sync(0xffffffffu, cur.live, l);
         if (!live) { done = true; break; }
@@ -321,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         ++n;
       }
-      cur = nxt;
+      cur = finish_batch(nxt);
       tb0 += batch_step;
     }
     // walk over: an end marker in the ring
