@@ -26,7 +26,7 @@
 //
 // Warp roles (one CTA per SM, 27 warps):
 //   warp 25     producer: walks the CTA's tiles, loads the per-tile scalars
-//               into a metadata ring, queues the TMA copies into a 6-stage
+//               into a metadata ring, queues the TMA copies into an 8-stage
 //               ring, zeroes the outputs of padding tiles;
 //   warp 26     staging: once a stage lands, permutes its scale factors into
 //               the tcgen05.cp layout and writes the fp32 k / q operands;
@@ -56,7 +56,7 @@ constexpr int kMmaWarp = 24;
 constexpr int kProdWarp = 25;
 constexpr int kStageWarp = 26;
 constexpr int kThreads = 27 * 32;
-constexpr int kStages = 6;
+constexpr int kStages = 8;
 constexpr int kRing = 16;  // metadata ring entries
 constexpr uint32_t kCodeBytes = kD * kD / 2;    // 8192
 constexpr uint32_t kScaleBytes = kD * kD / 16;  // 1024
