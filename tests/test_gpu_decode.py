@@ -212,6 +212,32 @@ def test_deterministic_bytes(cuda):
         assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("B", [4, 256])
+def test_back_to_back_steps_on_one_pool(cuda, B):
+    """Consecutive decode launches on one pool, queued back to back with no
+    host synchronisation, give the same bytes as the same steps with a
+    synchronisation after each.  The kernel is a programmatic dependent
+    launch whose set-up overlaps the previous launch: every step must still
+    read the state the previous step wrote."""
+    from gdn_b200 import ops
+    steps = 12
+    x = _inputs(B, steps, seed=21)
+    slot = torch.randperm(B, generator=torch.Generator().manual_seed(3)).to(torch.int32).cuda()
+    results = []
+    for sync_each in (True, False):
+        p, _ = _pool(B, 1, seed=4)
+        out = torch.empty((steps, B, HV, D), dtype=torch.bfloat16, device="cuda")
+        for t in range(steps):
+            ops.decode(x["q"][t], x["k"][t], x["v"][t], x["g"][t], x["beta"][t], slot, p, out=out[t])
+            if sync_each:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        results.append((out, p.codes.clone(), p.scales.clone(), p.gscale.clone()))
+    assert ops.device_status(clear=True) == 0
+    for a, b in zip(*results):
+        assert torch.equal(a, b)
+
+
 def test_full_size_batch256_with_random_slots(cuda, oracle_lib):
     """Batch-256 decode step over a 2048-slot pool addressed through a seeded
     random permutation: bit-exact codes against the reference quantiser on
