@@ -177,6 +177,24 @@ __device__ __forceinline__ float local_scale_fast(float amax) {
   return (amax > 0.0f) ? div6_for_scale(amax) : 1.0f;
 }
 
+// scale_encode(local_scale_fast(amax), mode) for a finite amax >= 0, without
+// the encoder's "<= 0 or not finite" test: amax / 6 of a finite amax is finite,
+// a quotient that underflows to 0 takes the subnormal branch to code 0 as the
+// test would, and a zero block takes the reference's local scale 1.0 (0x38).
+__device__ __forceinline__ uint32_t block_scale_code(float amax, int mode) {
+  if (!(amax > 0.0f)) return 0x38u;
+  const float x = div6_for_scale(amax);
+  if (x < 0.015625f) {
+    const int m = (int)__fmaf_rn(x, 512.0f, 0.5f);
+    return (uint32_t)(m > 7 ? 7 : m);
+  }
+  const uint32_t u = __float_as_uint(x);
+  const uint32_t add = ((u & 0x7FFFFFu) >= 0x700000u) ? 0x100000u : 0x80000u;
+  const uint32_t code = ((u + add) >> 20) - 960u;
+  const uint32_t sat = mode ? 0x7Eu : 0x77u;
+  return code > sat ? sat : code;
+}
+
 __device__ __forceinline__ float2 e2m1_nudge2(float2 v) {
   return __ffma2_rn(v, make_float2(-kE2M1TieEps, -kE2M1TieEps), v);
 }

@@ -89,7 +89,7 @@ __device__ __forceinline__ void requant_blocks(const float2 (&x)[8 * NB], const 
     const float am_y = __fmul_rn(am[blk], inv_gs);
     uint32_t w0, w1, sc;
     if (am_y <= 3.0e38f) {
-      sc = scale_encode(local_scale_fast(am_y), kMode);
+      sc = block_scale_code(am_y, kMode);
       const float inv = inv_tab[sc];
       const float2 inv2 = make_float2(inv, inv), zero2 = make_float2(0.0f, 0.0f);
       float2 nn[8];
