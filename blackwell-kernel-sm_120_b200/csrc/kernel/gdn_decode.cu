@@ -595,20 +595,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* dbg = kDebug ? a.debug_y + (((int64_t)m.b * a.HV + m.h) * kD + row) * kD + 64 * half : nullptr;
       uint32_t scw = 0;
 #pragma unroll
-      for (int blk = 0; blk < 4; ++blk) {
-        float2 x[8];
-        tc::ld_32x32b_x16(ta + 16 * blk, reinterpret_cast<float*>(x));
+      for (int bp = 0; bp < 2; ++bp) {  // two blocks per TMEM load and per 16-byte store
+        float2 x[16];
+        tc::ld_32x32b_x32(ta + 32 * bp, reinterpret_cast<float*>(x));
         tc::ld_wait();
-        if (blk == 3) {  // D1 is read: release it to the MMA warp
+        if (bp == 1) {  // D1 is read: release it to the MMA warp
           tc::fence_before_sync();
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.bar_q[grp]);
         }
-        const float a1[1] = {am[blk]};
-        uint32_t words[2], sc1;
-        requant_blocks<kMode, 1>(x, a1, mult, sm.inv_tab, words, sc1, kDebug ? dbg + 16 * blk : nullptr);
-        *reinterpret_cast<uint2*>(codes + 8 * blk) = make_uint2(words[0], words[1]);
-        scw |= sc1 << (8 * blk);
+        const float a2[2] = {am[2 * bp], am[2 * bp + 1]};
+        uint32_t words[4], sc2;
+        requant_blocks<kMode, 2>(x, a2, mult, sm.inv_tab, words, sc2, kDebug ? dbg + 32 * bp : nullptr);
+        *reinterpret_cast<uint4*>(codes + 16 * bp) = make_uint4(words[0], words[1], words[2], words[3]);
+        scw |= sc2 << (16 * bp);
       }
       *reinterpret_cast<uint32_t*>(a.pool_scales + m.pt * kScaleBytes + row * 8 + 4 * half) = scw;
       if (tid == lead) a.pool_gs[m.pt] = gs_new;
