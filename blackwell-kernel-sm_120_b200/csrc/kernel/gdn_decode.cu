@@ -65,7 +65,7 @@ constexpr uint32_t kStageTx = kCodeBytes + kScaleBytes + 3 * kVecBytes;
 constexpr float kDropBelow = 1e-30f;            // alpha * gs below this: the decayed state is zero
 
 // Named hardware barriers (0 is __syncthreads)
-constexpr int kBarQ0 = 1, kBarQ1 = 3, kBarW = 2;
+constexpr int kBarQ0 = 1, kBarQ1 = 3, kBarW = 2, kBarN = 4;
 
 // TMEM columns (512 allocated)
 constexpr uint32_t kTmemCols = 512;
@@ -95,6 +95,7 @@ struct __align__(1024) Stage {
   uint8_t sfp[kScaleBytes];   // scale factors in the tcgen05.cp 32x128b layout, 2 K-steps
   float4 kq4[kD / 2];         // (k_i, k_i+1, q_i, q_i+1), even i
   uint8_t ak[kD * 8 * 4];     // [128][8] fp32 K-major: columns 0, 1 = k, the rest 0
+  __nv_bfloat16 z[kD];        // the output gate (fused gated RMS norm only)
 };
 
 struct __align__(1024) DecodeSmem {
@@ -105,6 +106,7 @@ struct __align__(1024) DecodeSmem {
   float2 red[kD];               // partial [u p] / c of the second half of each row of D1'
   TileMeta ring[kRing];         // metadata of valid tile n at n % kRing
   uint32_t amax_bits[2][2];     // per group, per tile parity: tile max |D1| as float bits
+  float nrm[2][4];              // fused norm: per tile parity, per output warp, sum of x^2
   float inv_tab[256];
   uint64_t full[kStages], ready[kStages], empty[kStages];
   uint64_t bar_t, bar_tfree, bar_w[2], bar_d[2], bar_q[2], bar_fin;
@@ -149,6 +151,12 @@ struct DecodeArgs {
   const __nv_bfloat16* gate_b;
   int64_t gate_stride;
   int32_t qk_l2norm;
+  // fused gated RMS norm of the output (norm_weight == nullptr: plain output)
+  const float* norm_weight;
+  const __nv_bfloat16* gate_z;
+  int64_t z_stride;
+  float norm_eps;
+  int32_t norm_act;
 };
 
 // softplus(x) = log(1 + exp(x)), the identity above 20 (torch.nn.functional.softplus, beta 1).
@@ -173,7 +181,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&p);
 }
 
-template <int kMode, bool kDebug>
+static_assert(sizeof(Stage) == 16384, "a stage is 16 KB");
+
+template <int kMode, bool kDebug, bool kNorm>
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_decode_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_codes) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -322,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             m.end = 0;
             const int hk = h / a.group;
             uint64_t* bar = &sm.full[s];
-            mbar_arrive_expect_tx(bar, kStageTx);  // also publishes the metadata
+            mbar_arrive_expect_tx(bar, kStageTx + (kNorm && a.gate_z ? kVecBytes : 0u));  // also publishes the metadata
             asm volatile(
                 "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
                 "%3}], [%4];" ::"r"(smem_u32(st.codes)),
@@ -332,6 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bulk_g2s(st.q, a.q + b * a.q_stride + (int64_t)hk * kD, kVecBytes, bar);
             bulk_g2s(st.k, a.k + b * a.k_stride + (int64_t)hk * kD, kVecBytes, bar);
             bulk_g2s(st.v, a.v + b * a.v_stride + (int64_t)h * kD, kVecBytes, bar);
+            if (kNorm && a.gate_z) bulk_g2s(st.z, a.gate_z + b * a.z_stride + (int64_t)h * kD, kVecBytes, bar);
           }
         }
         ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -494,6 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3, half = (warp >> 2) & 1;
     const int j = 32 * quad + lane;
     const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
+    const float norm_wj = kNorm ? __ldg(a.norm_weight + j) : 0.0f;
     for (int n = 0;; ++n) {
       // one thread waits; the others sleep on the group's hardware barrier
       if (tid == 32 * kWWarp0) wait_bar(&sm.bar_t, (uint32_t)(n & 1), abort_flag);
@@ -535,7 +547,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float u = su.x + su.y + r.x, p = sp.x + sp.y + r.y;
       const float vj = bf2f(st.v[j]);
       const float wj = m.beta * (vj - c * u);
-      const float o = a.q_scale * fmaf(m.kq, wj, c * p);
+      float o = a.q_scale * fmaf(m.kq, wj, c * p);
+      if (kNorm) {
+        // gated RMS norm over the head (the 128 threads of the four half-0 warps):
+        // x = the bf16 output, x * rsqrt(mean(x^2) + eps) * weight * act(z)
+        const float x = __bfloat162float(__float2bfloat16_rn(o));
+        float sq = x * x;
+#pragma unroll
+        for (int s5 = 16; s5 > 0; s5 >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, s5);
+        if (lane == 0) sm.nrm[n & 1][quad] = sq;
+        named_bar(kBarN, 128);
+        const float* nr = sm.nrm[n & 1];
+        const float r = rsqrtf(((nr[0] + nr[1]) + (nr[2] + nr[3])) * (1.0f / kD) + a.norm_eps);
+        o = (x * r) * norm_wj;
+        if (a.gate_z) {
+          const float zf = bf2f(st.z[j]);
+          const float sg = 1.0f / (1.0f + expf(-zf));
+          o = o * (a.norm_act ? sg : zf * sg);
+        }
+      }
       const float o1 = __shfl_down_sync(0xffffffffu, o, 1);
       if ((j & 1) == 0)
         reinterpret_cast<uint32_t*>(a.out + ((int64_t)m.b * a.HV + m.h) * kD)[j >> 1] =
@@ -697,6 +727,17 @@ extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
   a.gate_stride = p->gate_stride ? p->gate_stride : p->num_v_heads;
   a.qk_l2norm = p->qk_l2norm;
   if (a.A_log && (!a.dt_bias || !a.gate_a || !a.gate_b || a.gate_stride < p->num_v_heads)) return GDN_ERR_ARGS;
+  a.norm_weight = p->norm_weight;
+  a.gate_z = p->norm_weight ? p->gate_z : nullptr;
+  a.z_stride = p->z_stride ? p->z_stride : (int64_t)p->num_v_heads * kD;
+  a.norm_eps = p->norm_eps;
+  a.norm_act = p->norm_act;
+  if (a.norm_weight) {
+    if (!(a.norm_eps > 0.0f && a.norm_eps < 1.0f) || (a.norm_act != 0 && a.norm_act != 1)) return GDN_ERR_ARGS;
+    if (p->debug_y) return GDN_ERR_UNSUPPORTED;  // the fused norm has no debug variant
+    if (a.gate_z && (!aligned16(a.gate_z) || a.z_stride % 8 || a.z_stride < (int64_t)p->num_v_heads * kD))
+      return GDN_ERR_ALIGN;
+  }
 
   CUtensorMap tm;
   {
@@ -717,15 +758,17 @@ extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
   const int64_t max_ctas = sm_count();
   const int grid = (int)(a.ntiles < max_ctas ? a.ntiles : max_ctas);
   // Opt in to > 48 KB of dynamic shared memory once per device and kernel.
-  static bool attr_set[4][64] = {};
+  static bool attr_set[6][64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GDN_ERR_CUDA;
-  const int mi = (p->scale_mode == kScaleRef240 ? 0 : 1) + (p->debug_y ? 2 : 0);
+  const int mi = (p->scale_mode == kScaleRef240 ? 0 : 1) + (p->debug_y ? 2 : 0) + (a.norm_weight ? 4 : 0);
   void (*kern)(const DecodeArgs, const CUtensorMap) =
-      mi == 0 ? gdn_decode_kernel<kScaleRef240, false>
-      : mi == 1 ? gdn_decode_kernel<kScaleFn448, false>
-      : mi == 2 ? gdn_decode_kernel<kScaleRef240, true>
-                : gdn_decode_kernel<kScaleFn448, true>;
+      mi == 0 ? gdn_decode_kernel<kScaleRef240, false, false>
+      : mi == 1 ? gdn_decode_kernel<kScaleFn448, false, false>
+      : mi == 2 ? gdn_decode_kernel<kScaleRef240, true, false>
+      : mi == 3 ? gdn_decode_kernel<kScaleFn448, true, false>
+      : mi == 4 ? gdn_decode_kernel<kScaleRef240, false, true>
+                : gdn_decode_kernel<kScaleFn448, false, true>;
   if (!attr_set[mi][dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return GDN_ERR_CUDA;

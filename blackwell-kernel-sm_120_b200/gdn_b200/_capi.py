@@ -65,6 +65,7 @@ class DecodeParams(ctypes.Structure):
         ("debug_y", _p),
         ("A_log", _p), ("dt_bias", _p), ("gate_a", _p), ("gate_b", _p), ("gate_stride", _i64),
         ("qk_l2norm", _i32),
+        ("norm_weight", _p), ("gate_z", _p), ("z_stride", _i64), ("norm_eps", _f32), ("norm_act", _i32),
     ]
 
 

@@ -126,7 +126,8 @@ def legacy_set_rounding(variant: int) -> int:
 # ---- decode ------------------------------------------------------------------------
 
 def decode(q, k, v, g, beta, slot_idx, pool, out=None, q_scale: float = 0.0, debug_y=None, *, A_log=None,
-           dt_bias=None, gate_a=None, gate_b=None, qk_l2norm: bool = False):
+           dt_bias=None, gate_a=None, gate_b=None, qk_l2norm: bool = False, norm_weight=None, gate_z=None,
+           norm_eps: float = 1e-6, norm_activation: str = "silu"):
     """One fused gated-delta-rule decode step over the NVFP4 pool `pool`
     (gdn_b200.pool.NVFP4StatePool).  q, k: [B, HK, D] bf16; v: [B, HV, D] bf16;
     g, beta: [B, HV] fp32; slot_idx: [B] int32.  Returns out [B, HV, D] bf16.
@@ -135,7 +136,13 @@ def decode(q, k, v, g, beta, slot_idx, pool, out=None, q_scale: float = 0.0, deb
     dt_bias ([HV] fp32) and the gate projections gate_a, gate_b ([B, HV] bf16),
     g = -exp(A_log) softplus(gate_a + dt_bias) and beta = sigmoid(gate_b) are
     computed in the kernel (g and beta may then be None); qk_l2norm scales q and
-    k to unit L2 norm per head in the kernel."""
+    k to unit L2 norm per head in the kernel.
+
+    Fused epilogue (vLLM's RMSNormGated, norm before gate, one group per
+    head): with norm_weight ([D], any float dtype), out holds
+    x * rsqrt(mean(x^2) + norm_eps) * norm_weight * act(gate_z) for the bf16
+    attention output x, act = SiLU ("silu" / "swish") or "sigmoid"; gate_z is
+    [B, HV, D] bf16 (or None: no gate).  The state update is unchanged."""
     B, HK, D = q.shape
     HV = v.shape[1]
     for t, name in ((q, "q"), (k, "k"), (v, "v")):
@@ -164,6 +171,17 @@ def decode(q, k, v, g, beta, slot_idx, pool, out=None, q_scale: float = 0.0, deb
         raise ValueError("shape mismatch")
     if pool.num_v_heads != HV or pool.head_dim != D:
         raise ValueError("pool does not match the head layout")
+    if norm_weight is not None:
+        if norm_weight.shape != (D,) or not norm_weight.is_cuda:
+            raise ValueError("norm_weight must be a CUDA [D] tensor")
+        norm_weight = norm_weight.to(torch.float32).contiguous()
+        if norm_activation not in ("silu", "swish", "sigmoid"):
+            raise ValueError(f"unsupported norm_activation {norm_activation!r}")
+        if gate_z is not None and (gate_z.dtype != torch.bfloat16 or not gate_z.is_cuda or gate_z.shape != (B, HV, D)
+                                   or gate_z.stride(-1) != 1 or gate_z.stride(-2) != D):
+            raise ValueError("gate_z must be CUDA bf16 [B, HV, D] with contiguous heads")
+        if debug_y is not None:
+            raise ValueError("debug_y is not available with the fused norm")
     if out is None:
         out = torch.empty((B, HV, D), dtype=torch.bfloat16, device=q.device)
     p = _capi.DecodeParams()
@@ -182,6 +200,11 @@ def decode(q, k, v, g, beta, slot_idx, pool, out=None, q_scale: float = 0.0, deb
         p.A_log, p.dt_bias = A_log.data_ptr(), dt_bias.data_ptr()
         p.gate_a, p.gate_b, p.gate_stride = gate_a.data_ptr(), gate_b.data_ptr(), gate_a.stride(0)
     p.qk_l2norm = 1 if qk_l2norm else 0
+    if norm_weight is not None:
+        p.norm_weight = norm_weight.data_ptr()
+        p.gate_z, p.z_stride = (gate_z.data_ptr(), gate_z.stride(0)) if gate_z is not None else (None, 0)
+        p.norm_eps = norm_eps
+        p.norm_act = 1 if norm_activation == "sigmoid" else 0
     check("gdn_decode", lib.gdn_decode(ctypes.byref(p), _stream(q)))
     return out
 

@@ -170,6 +170,18 @@ typedef struct gdn_decode_params {
   const gdn_bf16_t* gate_b; /* [B, HV], sequence stride gate_stride */
   int64_t gate_stride;      /* elements between sequences; 0 = HV */
   int32_t qk_l2norm;        /* != 0: q and k scaled to unit L2 norm per head, x / sqrt(sum x^2 + 1e-6), in fp32 */
+  /* Optional fused epilogue: the gated RMS norm vLLM's GDN layer applies to
+   * the attention output before its out-projection (RMSNormGated with
+   * norm_before_gate, one group per head).  With norm_weight set, out holds
+   *   x * rsqrt(mean_d(x^2) + norm_eps) * norm_weight[d] * act(z[b, h, d])
+   * where x is the bf16 attention output and act is SiLU (norm_act 0) or the
+   * sigmoid (1); with gate_z NULL there is no gate.  fp32 arithmetic, bf16
+   * result.  The state update is unchanged. */
+  const float* norm_weight; /* [D] or NULL */
+  const gdn_bf16_t* gate_z; /* [B, HV, D], sequence stride z_stride, or NULL */
+  int64_t z_stride;         /* elements between sequences (a multiple of 8); 0 = HV * D */
+  float norm_eps;           /* > 0 */
+  int32_t norm_act;         /* 0: SiLU, 1: sigmoid */
 } gdn_decode_params;
 
 GDN_API int gdn_decode(const gdn_decode_params* params, cudaStream_t stream);
