@@ -65,7 +65,7 @@ constexpr uint32_t kStageTx = kCodeBytes + kScaleBytes + 3 * kVecBytes;
 constexpr float kDropBelow = 1e-30f;            // alpha * gs below this: the decayed state is zero
 
 // Named hardware barriers (0 is __syncthreads)
-constexpr int kBarQ0 = 1, kBarQ1 = 3, kBarW = 2, kBarN = 4;
+constexpr int kBarQ0 = 1, kBarQ1 = 3, kBarW = 2;
 
 // TMEM columns (512 allocated)
 constexpr uint32_t kTmemCols = 512;
@@ -506,11 +506,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int j = 32 * quad + lane;
     const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
     const float norm_wj = kNorm ? __ldg(a.norm_weight + j) : 0.0f;
+    // Fused norm: tile n's normed output is stored after tile n + 1's first
+    // barrier, which is also where every half-0 warp's sum of x^2 for tile n is
+    // visible (no barrier of its own): x, z and the row are carried over.
+    float pend_x = 0.0f, pend_z = 0.0f;
+    int64_t pend_row = -1;
+    auto flush_norm = [&](int np) {
+      if (!kNorm || half || pend_row < 0) return;
+      const float* nr = sm.nrm[np & 1];
+      const float r = rsqrtf(((nr[0] + nr[1]) + (nr[2] + nr[3])) * (1.0f / kD) + a.norm_eps);
+      float y = (pend_x * r) * norm_wj;
+      if (a.gate_z) {
+        const float sg = 1.0f / (1.0f + expf(-pend_z));
+        y = y * (a.norm_act ? sg : pend_z * sg);
+      }
+      const float y1 = __shfl_down_sync(0xffffffffu, y, 1);
+      if ((j & 1) == 0) reinterpret_cast<uint32_t*>(a.out + pend_row * kD)[j >> 1] = pack_bf16x2(y, y1);
+      pend_row = -1;
+    };
     for (int n = 0;; ++n) {
       // one thread waits; the others sleep on the group's hardware barrier
       if (tid == 32 * kWWarp0) wait_bar(&sm.bar_t, (uint32_t)(n & 1), abort_flag);
       named_bar(kBarW, 256);
       if (*abort_flag) break;
+      flush_norm(n - 1);
       const TileMeta m = sm.ring[n % kRing];
       if (m.end) break;
       const Stage& st = sm.st[n % kStages];
@@ -547,29 +566,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float u = su.x + su.y + r.x, p = sp.x + sp.y + r.y;
       const float vj = bf2f(st.v[j]);
       const float wj = m.beta * (vj - c * u);
-      float o = a.q_scale * fmaf(m.kq, wj, c * p);
+      const float o = a.q_scale * fmaf(m.kq, wj, c * p);
       if (kNorm) {
-        // gated RMS norm over the head (the 128 threads of the four half-0 warps):
-        // x = the bf16 output, x * rsqrt(mean(x^2) + eps) * weight * act(z)
-        const float x = __bfloat162float(__float2bfloat16_rn(o));
-        float sq = x * x;
+        // gated RMS norm over the head: x = the bf16 output; this warp's sum of
+        // x^2 now, x * rsqrt(mean(x^2) + eps) * weight * act(z) after the next barrier
+        pend_x = __bfloat162float(__float2bfloat16_rn(o));
+        pend_z = a.gate_z ? bf2f(st.z[j]) : 0.0f;
+        pend_row = (int64_t)m.b * a.HV + m.h;
+        float sq = pend_x * pend_x;
 #pragma unroll
         for (int s5 = 16; s5 > 0; s5 >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, s5);
         if (lane == 0) sm.nrm[n & 1][quad] = sq;
-        named_bar(kBarN, 128);
-        const float* nr = sm.nrm[n & 1];
-        const float r = rsqrtf(((nr[0] + nr[1]) + (nr[2] + nr[3])) * (1.0f / kD) + a.norm_eps);
-        o = (x * r) * norm_wj;
-        if (a.gate_z) {
-          const float zf = bf2f(st.z[j]);
-          const float sg = 1.0f / (1.0f + expf(-zf));
-          o = o * (a.norm_act ? sg : zf * sg);
-        }
+      } else {
+        const float o1 = __shfl_down_sync(0xffffffffu, o, 1);
+        if ((j & 1) == 0)
+          reinterpret_cast<uint32_t*>(a.out + ((int64_t)m.b * a.HV + m.h) * kD)[j >> 1] =
+              pack_bf16x2(o, o1);  // one paired conversion (faster than two single ones)
       }
-      const float o1 = __shfl_down_sync(0xffffffffu, o, 1);
-      if ((j & 1) == 0)
-        reinterpret_cast<uint32_t*>(a.out + ((int64_t)m.b * a.HV + m.h) * kD)[j >> 1] =
-            pack_bf16x2(o, o1);  // one paired conversion (faster than two single ones)
       const float wc = wj * m.inv_c;
       const float hi = __uint_as_float(__float_as_uint(wc) & 0xFFFFE000u);
       uint8_t* bw = sm.bw[n & 1];
