@@ -610,18 +610,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (m.end) break;
       tc::fence_after_sync();
       const uint32_t ta = T + lane_base + kColD1 + 128 * grp + 64 * half;
-      // pass 1: block maxima of this thread's 64 values
+      // pass 1: block maxima of this thread's 64 values, columns 32-63 first; columns
+      // 0-31 stay in registers for pass 2
       float am[4];
       float tmax = 0.0f;
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
+      float2 x0[16];
+      {
         float2 x[16];
-        tc::ld_32x32b_x32(ta + 32 * h2, reinterpret_cast<float*>(x));
+        tc::ld_32x32b_x32(ta + 32, reinterpret_cast<float*>(x));
         tc::ld_wait();
         float a2[2];
-        tmax = fmaxf(tmax, block_amax3<2>(x, a2));
-        am[2 * h2] = a2[0];
-        am[2 * h2 + 1] = a2[1];
+        tmax = block_amax3<2>(x, a2);
+        am[2] = a2[0];
+        am[3] = a2[1];
+      }
+      {
+        tc::ld_32x32b_x32(ta, reinterpret_cast<float*>(x0));
+        tc::ld_wait();
+        float a2[2];
+        tmax = fmaxf(tmax, block_amax3<2>(x0, a2));
+        am[0] = a2[0];
+        am[1] = a2[1];
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
@@ -640,9 +649,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int bp = 0; bp < 2; ++bp) {  // two blocks per TMEM load and per 16-byte store
         float2 x[16];
-        tc::ld_32x32b_x32(ta + 32 * bp, reinterpret_cast<float*>(x));
-        tc::ld_wait();
-        if (bp == 1) {  // D1 is read: release it to the MMA warp
+        if (bp == 0) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) x[e] = x0[e];
+        } else {
+          tc::ld_32x32b_x32(ta + 32, reinterpret_cast<float*>(x));
+          tc::ld_wait();
+          // D1 is read: release it to the MMA warp
           tc::fence_before_sync();
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.bar_q[grp]);
