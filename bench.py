@@ -39,7 +39,6 @@ import json
 import math
 import os
 import pathlib
-import re
 import statistics
 import sys
 import threading
@@ -160,6 +159,31 @@ def _max_over_ranks(dist, x: float) -> float:
     return sharding.max_over_ranks(x)
 
 
+def _rank_spread(dist, ms_per_step: float) -> dict | None:
+    """min / median / max of the ranks' own ms per step (every rank takes part)."""
+    if dist is None:
+        return None
+    import torch
+    world = dist.get_world_size()
+    t = torch.tensor([ms_per_step], dtype=torch.float64, device="cuda")
+    parts = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(parts, t)
+    vals = [float(x.item()) for x in parts]
+    return {"min": round(min(vals), 5), "median": round(statistics.median(vals), 5), "max": round(max(vals), 5),
+            "slowest_rank": int(max(range(world), key=lambda r: vals[r]))}
+
+
+def _workloads():
+    """gdn_b200/workloads.py loaded by its path: the seeded synthetic inputs,
+    without importing the gdn_b200 package (whose import loads the CUDA
+    library), so that the CPU legs map no product code."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("gdn_bench_workloads", PKG / "gdn_b200" / "workloads.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
 # ---- CPU path ---------------------------------------------------------------------------------
 
 class CpuDecode:
@@ -167,12 +191,11 @@ class CpuDecode:
     sequences (all 32 heads each) of the batch-256 decode step, set up once so
     that every timed pass runs on warm buffers."""
 
-    sample_seqs = 16
-
-    def __init__(self, threads: int | None = None):
+    def __init__(self, threads: int | None = None, sample_seqs: int = 16):
+        self.sample_seqs = sample_seqs
         import numpy as np
-        from gdn_b200 import workloads
         from oracle import bindings as ob
+        workloads = _workloads()
 
         self.lib, self.kind = ob.cpu_baseline(prefer_reference=True)
         # the reference host codec saturates scales at 240: pair it with gs = amax/(6*240)
@@ -228,16 +251,6 @@ def cpu_decode_sample(seconds: float, threads: int | None = None) -> dict:
 
 # ---- GPU path ---------------------------------------------------------------------------------------
 
-def _traffic_from_profile(summary: str) -> float | None:
-    """DRAM bytes (read + write) per launch, from the `dram_bytes_per_launch = N`
-    line of an ncu summary under profiles/ (null when there is none)."""
-    p = ROOT / "profiles" / summary
-    if not p.exists():
-        return None
-    m = re.search(r"^dram_bytes_per_launch = (\d+)", p.read_text(), re.M)
-    return float(m.group(1)) if m else None
-
-
 def run_ours(args, dist, rank, world, local) -> dict | None:
     import torch
     from gdn_b200 import NVFP4StatePool, ops, workloads
@@ -285,7 +298,9 @@ def run_ours(args, dist, rank, world, local) -> dict | None:
         t_end.record(stream)
         torch.cuda.synchronize()
     _barrier(dist)
-    total_ms = _max_over_ranks(dist, t_begin.elapsed_time(t_end))
+    own_ms = t_begin.elapsed_time(t_end)
+    total_ms = _max_over_ranks(dist, own_ms)
+    spread = _rank_spread(dist, own_ms / args.steps)
     mean_launch_ms = total_ms / args.steps
     if ops.device_status(clear=True):
         raise RuntimeError("device status set during the timed region")
@@ -394,12 +409,15 @@ def run_ours(args, dist, rank, world, local) -> dict | None:
         "e2e": {"value": round(B * world * e2e_steps / (e2e_ms / 1e3), 1), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": _traffic_from_profile("gdn_decode_b256.md"),
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "traffic_note": "not measured in this run; ncu DRAM bytes of one launch are in profiles/",
                      "peak_source": peak_note, "kernel": "gdn_decode_kernel",
                      "mean_launch_us": round(mean_launch_ms * 1e3, 3)},
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
     }
+    if spread is not None:
+        line["per_rank_ms_per_step"] = spread
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_decode_sample(args.cpu_seconds)
     return line
@@ -442,7 +460,12 @@ def _timed(args, dist, stream, step, local):
     _barrier(dist)
     if ops.device_status(clear=True):
         raise RuntimeError("device status set during the timed region")
-    return _max_over_ranks(dist, t0.elapsed_time(t1)), clocks.summary()
+    own = t0.elapsed_time(t1)
+    summary = clocks.summary()
+    spread = _rank_spread(dist, own / args.steps)
+    if spread is not None:
+        summary = dict(summary, per_rank_ms_per_step=spread)
+    return _max_over_ranks(dist, own), summary
 
 
 def _kernel_ms(args, stream, launch, reps: int = 5) -> float:
@@ -518,7 +541,7 @@ def run_prefill(args, dist, rank, world, local) -> dict | None:
         "e2e": {"value": round(tokens / (e_ms / 1e3), 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": host_out.numel() * 2},
         "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": tpeak, "unit": "TFLOP/s",
-                     "frac": round(tf / tpeak, 4), "traffic": _traffic_from_profile("gdn_prefill_8x8192.md"), "kernel": "gdn_prefill_kernel",
+                     "frac": round(tf / tpeak, 4), "traffic": None, "kernel": "gdn_prefill_kernel",
                      "mean_launch_us": round(launch_ms * 1e3, 2),
                      "hbm": {"achieved": round(gbs, 1), "peak": hpeak, "frac": round(gbs / hpeak, 4)}},
         "gpu_launches": args.steps, "clocks": clocks})
@@ -641,7 +664,8 @@ def run_layers(args, dist, rank, world, local) -> dict | None:
 def run_reference(args, rank) -> dict | None:
     if rank != 0:
         return None
-    cpu = CpuDecode()
+    # each step is a 64-sequence sample (all 32 heads), ~50 ms on 16 host threads
+    cpu = CpuDecode(sample_seqs=64)
     for _ in range(args.warmup):
         cpu.run_pass()
     # each step: one pass over the 16-sequence sample; value: tokens/s over the timed steps
@@ -651,11 +675,15 @@ def run_reference(args, rank) -> dict | None:
     el = time.perf_counter() - t0
     value = args.steps * cpu.sample_seqs / el
     cb = {"value": round(value, 2), "unit": UNIT, "cores": cpu.threads, "kind": cpu.kind,
-          "sample": "each step: one pass of the decode step over a 16-sequence sample; " + cpu.describe(args.steps, el)}
+          "sample": f"each step: one pass of the decode step over a {cpu.sample_seqs}-sequence sample; "
+          + cpu.describe(args.steps, el)}
     return {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32 math, nvfp4 state, bf16 io", "data": "synthetic",
             "config": _config(args.gpus), "impl": "reference", "cpu_baseline": cb,
+            "scale_mode_note": ("the reference's NVFP4 codec has no E4M3FN-range mode (its scale encoder saturates "
+                                "at 240), so this arm runs it with gs = amax/(6*240); the per-element work equals "
+                                "the fn448 arm's" if cpu.kind == "reference" else "oracle port, fn448"),
             "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "gpu_launches": 0}
 

@@ -115,12 +115,19 @@ def build_torch_op(verbose: bool = False) -> pathlib.Path | None:
     return so
 
 
+def reference_dir() -> pathlib.Path:
+    """The reference checkout: $GDN_REFERENCE_DIR, else a checkout named
+    `reference` beside this repository."""
+    env = os.environ.get("GDN_REFERENCE_DIR")
+    return pathlib.Path(env) if env else ROOT.parent / "reference"
+
+
 def build_oracle(verbose: bool = False) -> None:
     """The CPU oracle (test infrastructure); the reference leg only where the
     reference checkout exists."""
     oracle = ROOT / "oracle"
     _run(["make", "-C", oracle, "-s"], verbose)
-    ref = pathlib.Path(os.environ.get("GDN_REFERENCE_DIR", "/root/reference"))
+    ref = reference_dir()
     if (ref / "src" / "kernel" / "gdn_state_update_ref.cu").exists():
         _run(["make", "-C", oracle, "-s", "ref", f"REF={ref}"], verbose)
 

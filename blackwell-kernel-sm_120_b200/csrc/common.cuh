@@ -118,4 +118,9 @@ inline int launch_status() {
 // SM count of the current device (cached per device).
 int sm_count();
 
+// Raises `func`'s dynamic shared-memory limit to `bytes` on the current
+// device, once per (kernel, device); safe to call from any host thread.
+// Returns GDN_OK or GDN_ERR_CUDA.
+int allow_dynamic_smem(const void* func, int bytes);
+
 }  // namespace gdn

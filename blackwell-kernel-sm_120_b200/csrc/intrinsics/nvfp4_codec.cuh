@@ -221,6 +221,19 @@ __device__ __forceinline__ uint32_t cvt_e2m1x8(const float* n) {
   return r;
 }
 
+// E2M1 codes of v = RN(y * inv) for 8 values (pairs y[0..3], element 0 in the
+// low nibble) with the reference's rounding: nearest, ties to the smaller
+// magnitude, sign from (v < 0).  The nudge also maps v = -0 to +0 (code 0x0),
+// as the reference's sign test does.  Exact for every finite y * inv with
+// |v| < 8 (larger values saturate to 6 either way); the whole domain is swept
+// by gdn_b200_selftest_codec.
+__device__ __forceinline__ uint32_t e2m1_encode8(const float2* y, float2 inv2) {
+  float2 n[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) n[p] = e2m1_nudge2(__fmul2_rn(y[p], inv2));
+  return cvt_e2m1x8(reinterpret_cast<const float*>(n));
+}
+
 // One code word (8 nibbles, element 0 in the low nibble) -> 8 raw E2M1 values as
 // four f16x2 (element 2j in the low half of out[j]).  Exact.
 __device__ __forceinline__ void cvt_e2m1x8_to_f16x2(uint32_t w, uint32_t (&out)[4]) {
@@ -303,11 +316,12 @@ __device__ __forceinline__ uint32_t quantize16(const float* y, float amax_nan, i
   float inv = scale_inverse(scale_decode(sc, mode));
   if (kCheckRange) fast = fast && (amax_ok * inv < 16777216.0f);
   if (fast) {
-    float n[16];
+    float2 yp[8];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) n[i] = e2m1_nudge(__fmaf_rn(y[i], inv, 0.0f));
-    w0 = cvt_e2m1x8(n);
-    w1 = cvt_e2m1x8(n + 8);
+    for (int p = 0; p < 8; ++p) yp[p] = make_float2(y[2 * p], y[2 * p + 1]);
+    const float2 inv2 = make_float2(inv, inv);
+    w0 = e2m1_encode8(yp, inv2);
+    w1 = e2m1_encode8(yp + 4, inv2);
     return sc;
   }
   return quantize16_exact(y, mode, w0, w1);

@@ -730,6 +730,10 @@ extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
       !aligned16(p->pool_scales) || !aligned16(p->out) || (a.q_stride | a.k_stride | a.v_stride) % 8 ||
       (p->debug_y && !aligned16(p->debug_y)))
     return GDN_ERR_ALIGN;
+  // A sequence's q/k/v rows must not overlap the next sequence's.
+  if (a.q_stride < (int64_t)p->num_k_heads * kD || a.k_stride < (int64_t)p->num_k_heads * kD ||
+      a.v_stride < (int64_t)p->num_v_heads * kD)
+    return GDN_ERR_ARGS;
   // The codes are addressed as rows of a 2-D tensor map (int32 row coordinate).
   if (a.ntiles > INT32_MAX || p->num_slots * (int64_t)p->num_v_heads * kD > INT32_MAX) return GDN_ERR_UNSUPPORTED;
   a.g = p->g;
@@ -783,10 +787,6 @@ extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
   const int smem = (int)sizeof(DecodeSmem);
   const int64_t max_ctas = sm_count();
   const int grid = (int)(a.ntiles < max_ctas ? a.ntiles : max_ctas);
-  // Opt in to > 48 KB of dynamic shared memory once per device and kernel.
-  static bool attr_set[6][64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GDN_ERR_CUDA;
   const int mi = (p->scale_mode == kScaleRef240 ? 0 : 1) + (p->debug_y ? 2 : 0) + (a.norm_weight ? 4 : 0);
   void (*kern)(const DecodeArgs, const CUtensorMap) =
       mi == 0 ? gdn_decode_kernel<kScaleRef240, false, false>
@@ -795,11 +795,8 @@ extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
       : mi == 3 ? gdn_decode_kernel<kScaleFn448, true, false>
       : mi == 4 ? gdn_decode_kernel<kScaleRef240, false, true>
                 : gdn_decode_kernel<kScaleFn448, false, true>;
-  if (!attr_set[mi][dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return GDN_ERR_CUDA;
-    attr_set[mi][dev] = true;
-  }
+  // > 48 KB of dynamic shared memory: opted in once per (kernel, device), under a lock.
+  if (allow_dynamic_smem(reinterpret_cast<const void*>(kern), smem) != GDN_OK) return GDN_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(kThreads);

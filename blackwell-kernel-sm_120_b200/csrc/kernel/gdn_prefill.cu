@@ -937,18 +937,10 @@ extern "C" int gdn_prefill(const gdn_prefill_params* p, cudaStream_t stream) {
   const int smem = (int)kSmemBytes;
   const int64_t max_ctas = sm_count();
   const int grid = (int)(nitems < max_ctas ? nitems : max_ctas);
-  static bool attr_set[2][64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GDN_ERR_CUDA;
   const int mi = p->scale_mode == kScaleRef240 ? 0 : 1;
-  if (!attr_set[mi][dev]) {
-    const cudaError_t e = mi == 0 ? cudaFuncSetAttribute(gdn_prefill_kernel<kScaleRef240>,
-                                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
-                                  : cudaFuncSetAttribute(gdn_prefill_kernel<kScaleFn448>,
-                                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return GDN_ERR_CUDA;
-    attr_set[mi][dev] = true;
-  }
+  const void* kern = mi == 0 ? reinterpret_cast<const void*>(gdn_prefill_kernel<kScaleRef240>)
+                             : reinterpret_cast<const void*>(gdn_prefill_kernel<kScaleFn448>);
+  if (allow_dynamic_smem(kern, smem) != GDN_OK) return GDN_ERR_CUDA;
   if (mi == 0)
     gdn_prefill_kernel<kScaleRef240><<<grid, kThreads, smem, stream>>>(a, tq, tk, tv);
   else

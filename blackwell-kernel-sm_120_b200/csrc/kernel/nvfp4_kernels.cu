@@ -213,13 +213,14 @@ __global__ void __launch_bounds__(kThreads) legacy_update_kernel(const uint8_t* 
 
 // fmaf(beta*k, v, alpha*s): the rounding of the reference's compiled update
 // line, found by comparing every variant bit for bit with the reference's
-// launch_gdn_ref on a B200 (tests/test_gpu_legacy.py).
-int g_legacy_variant = 1;
+// launch_gdn_ref on a B200 (tests/test_gpu_legacy.py).  The reference entry
+// points always use it; gdn_legacy_update_rounding takes a variant per call.
+constexpr int kLegacyReferenceVariant = 1;
 
 template <bool kOutF32>
 int launch_legacy(const uint8_t* S_data, const uint8_t* S_scales, const __nv_bfloat16* k,
                   const __nv_bfloat16* v, uint8_t* out_data, uint8_t* out_scales, float* out_f32,
-                  float alpha, float beta, int d, cudaStream_t stream) {
+                  float alpha, float beta, int d, int variant, cudaStream_t stream) {
   const int64_t n = (int64_t)d * d;
   const int64_t nblk = n / 16;
   const int grid = grid_for(nblk);
@@ -227,7 +228,7 @@ int launch_legacy(const uint8_t* S_data, const uint8_t* S_scales, const __nv_bfl
   legacy_update_kernel<V, kOutF32, A><<<grid, kThreads, 0, stream>>>(S_data, S_scales, k, v, out_data, \
                                                                      out_scales, out_f32, alpha, beta, d, nblk)
   const bool aligned_rows = (d % 16 == 0) && aligned16(v);
-  switch (g_legacy_variant * 2 + (aligned_rows ? 1 : 0)) {
+  switch (variant * 2 + (aligned_rows ? 1 : 0)) {
     case 0: GDN_LEGACY_LAUNCH(0, false); break;
     case 1: GDN_LEGACY_LAUNCH(0, true); break;
     case 2: GDN_LEGACY_LAUNCH(1, false); break;
@@ -237,6 +238,36 @@ int launch_legacy(const uint8_t* S_data, const uint8_t* S_scales, const __nv_bfl
   }
 #undef GDN_LEGACY_LAUNCH
   return launch_status();
+}
+
+// Sweeps of the device codec over consecutive fp32 bit patterns lo, lo+1, ...
+// (the exhaustive checks of the production paths against the reference):
+//   which 0: out[i] = block_scale_code(f, mode), the scale byte the
+//            requantisers write for a block whose max |y| is f;
+//   which 1: out[i] = e2m1_encode8 nibble of f with inverse scale 1, the
+//            per-element encoder every quantiser here uses.
+// One thread per 8 values; the caller keeps lo + count <= 2^32.
+__global__ void __launch_bounds__(kThreads) codec_selftest_kernel(int which, uint32_t lo, int64_t count, int mode,
+                                                                  uint8_t* __restrict__ out) {
+  for (int64_t t = blockIdx.x * (int64_t)kThreads + threadIdx.x; t * 8 < count; t += (int64_t)gridDim.x * kThreads) {
+    const int64_t i0 = t * 8;
+    const int n = count - i0 < 8 ? (int)(count - i0) : 8;
+    float f[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(lo + (uint32_t)(i0 + (e < n ? e : 0)));
+    uint8_t r[8];
+    if (which == 0) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) r[e] = (uint8_t)block_scale_code(f[e], mode);
+    } else {
+      const float2 y[4] = {make_float2(f[0], f[1]), make_float2(f[2], f[3]), make_float2(f[4], f[5]),
+                           make_float2(f[6], f[7])};
+      const uint32_t w = e2m1_encode8(y, make_float2(1.0f, 1.0f));
+#pragma unroll
+      for (int e = 0; e < 8; ++e) r[e] = (uint8_t)((w >> (4 * e)) & 0xFu);
+    }
+    for (int e = 0; e < n; ++e) out[i0 + e] = r[e];
+  }
 }
 
 bool legacy_args_ok(const void* a, const void* b, const void* k, const void* v, const void* c,
@@ -249,12 +280,6 @@ bool legacy_args_ok(const void* a, const void* b, const void* k, const void* v, 
 
 using namespace gdn;
 
-extern "C" int gdn_legacy_set_rounding(int variant) {
-  const int prev = g_legacy_variant;
-  if (variant >= 0 && variant <= 2) g_legacy_variant = variant;
-  return prev;
-}
-
 extern "C" int launch_gdn_state_update(const uint8_t* S_data, const uint8_t* S_scales, const __nv_bfloat16* k,
                                        const __nv_bfloat16* v, uint8_t* S_out_data, uint8_t* S_out_scales,
                                        float alpha, float beta, int d, cudaStream_t stream) {
@@ -265,7 +290,7 @@ extern "C" int launch_gdn_state_update(const uint8_t* S_data, const uint8_t* S_s
   if ((reinterpret_cast<uintptr_t>(S_data) & 7u) || (reinterpret_cast<uintptr_t>(S_out_data) & 7u))
     return GDN_ERR_ALIGN;
   return launch_legacy<false>(S_data, S_scales, k, v, S_out_data, S_out_scales, nullptr, alpha, beta, d,
-                              stream);
+                              kLegacyReferenceVariant, stream);
 }
 
 extern "C" void launch_gdn_ref(const uint8_t* S_data, const uint8_t* S_scales, const __nv_bfloat16* k,
@@ -273,7 +298,26 @@ extern "C" void launch_gdn_ref(const uint8_t* S_data, const uint8_t* S_scales, c
                                cudaStream_t stream) {
   if (!legacy_args_ok(S_data, S_scales, k, v, S_out, S_out, d)) return;
   if ((reinterpret_cast<uintptr_t>(S_data) & 7u) || !aligned16(S_out)) return;
-  launch_legacy<true>(S_data, S_scales, k, v, nullptr, nullptr, S_out, alpha, beta, d, stream);
+  launch_legacy<true>(S_data, S_scales, k, v, nullptr, nullptr, S_out, alpha, beta, d, kLegacyReferenceVariant,
+                      stream);
+}
+
+extern "C" int gdn_legacy_update_rounding(const uint8_t* S_data, const uint8_t* S_scales, const __nv_bfloat16* k,
+                                          const __nv_bfloat16* v, uint8_t* S_out_data, uint8_t* S_out_scales,
+                                          float* S_out_f32, float alpha, float beta, int d, int rounding,
+                                          cudaStream_t stream) {
+  if (rounding < 0 || rounding > 2) return GDN_ERR_ARGS;
+  if (S_out_f32) {
+    if (!legacy_args_ok(S_data, S_scales, k, v, S_out_f32, S_out_f32, d)) return GDN_ERR_ARGS;
+    if ((reinterpret_cast<uintptr_t>(S_data) & 7u) || !aligned16(S_out_f32)) return GDN_ERR_ALIGN;
+    return launch_legacy<true>(S_data, S_scales, k, v, nullptr, nullptr, S_out_f32, alpha, beta, d, rounding,
+                               stream);
+  }
+  if (!legacy_args_ok(S_data, S_scales, k, v, S_out_data, S_out_scales, d)) return GDN_ERR_ARGS;
+  if ((reinterpret_cast<uintptr_t>(S_data) & 7u) || (reinterpret_cast<uintptr_t>(S_out_data) & 7u))
+    return GDN_ERR_ALIGN;
+  return launch_legacy<false>(S_data, S_scales, k, v, S_out_data, S_out_scales, nullptr, alpha, beta, d, rounding,
+                              stream);
 }
 
 extern "C" int gdn_nvfp4_quantize(const float* x, uint8_t* codes, uint8_t* scales, int64_t n, int32_t mode,
@@ -336,5 +380,15 @@ extern "C" int gdn_nvfp4_dequantize_tiles(const uint8_t* codes, const uint8_t* s
   else
     dequantize_tiles_kernel<kScaleFn448><<<grid_for(nblk), kThreads, 0, stream>>>(codes, scales, gscale,
                                                                                   tile_elems / 16, out, nblk);
+  return launch_status();
+}
+
+extern "C" int gdn_b200_selftest_codec(int32_t which, uint32_t lo_bits, int64_t count, int32_t scale_mode,
+                                       uint8_t* out, cudaStream_t stream) {
+  if (!out || count <= 0 || (which != 0 && which != 1)) return GDN_ERR_ARGS;
+  if ((uint64_t)lo_bits + (uint64_t)count > (1ull << 32)) return GDN_ERR_ARGS;
+  if (scale_mode != kScaleRef240 && scale_mode != kScaleFn448) return GDN_ERR_UNSUPPORTED;
+  const int64_t threads = (count + 7) / 8;
+  codec_selftest_kernel<<<grid_for(threads), kThreads, 0, stream>>>(which, lo_bits, count, scale_mode, out);
   return launch_status();
 }

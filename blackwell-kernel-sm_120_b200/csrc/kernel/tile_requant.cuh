@@ -91,12 +91,9 @@ __device__ __forceinline__ void requant_blocks(const float2 (&x)[8 * NB], const 
     if (am_y <= 3.0e38f) {
       sc = block_scale_code(am_y, kMode);
       const float inv = inv_tab[sc];
-      const float2 inv2 = make_float2(inv, inv), zero2 = make_float2(0.0f, 0.0f);
-      float2 nn[8];
-#pragma unroll
-      for (int p = 0; p < 8; ++p) nn[p] = e2m1_nudge2(__ffma2_rn(y[p], inv2, zero2));
-      w0 = cvt_e2m1x8(reinterpret_cast<const float*>(nn));
-      w1 = cvt_e2m1x8(reinterpret_cast<const float*>(nn + 4));
+      const float2 inv2 = make_float2(inv, inv);
+      w0 = e2m1_encode8(y, inv2);
+      w1 = e2m1_encode8(y + 4, inv2);
     } else {  // NaN or inf in the block: exact scalar path
       sc = quantize16_exact_pairs(y, kMode, w0, w1);
     }

@@ -32,11 +32,13 @@ __global__ void __launch_bounds__(kThreads) pool_copy_kernel(const uint8_t* __re
                                                              float* __restrict__ dst_gs,
                                                              const int32_t* __restrict__ slot_idx,
                                                              int64_t num_slots, int32_t HV, int64_t code_rec,
-                                                             int64_t scale_rec, int32_t n) {
+                                                             int64_t scale_rec, int32_t n, uint32_t* status) {
   const int i = blockIdx.y;
   if (i >= n) return;
   const int32_t slot = __ldg(slot_idx + i);
   const bool valid = slot >= 0 && slot < num_slots;
+  // a slot past the pool is treated as padding and reported
+  if (slot >= num_slots && blockIdx.x == 0 && threadIdx.x == 0) atomicOr(status, kStatusBadSlot);
   if (!valid && !kGather) return;  // scatter: padding rows are skipped
   // Gather reads pool[slot] into dense[i]; scatter reads dense[i] into pool[slot].
   const int64_t src_rec = kGather ? (int64_t)slot : (int64_t)i;
@@ -68,6 +70,8 @@ int pool_copy(bool gather, const uint8_t* sc, const uint8_t* ss, const float* sg
   if (D % 16) return GDN_ERR_UNSUPPORTED;
   if (!aligned16(sc) || !aligned16(ss) || !aligned16(dc) || !aligned16(ds)) return GDN_ERR_ALIGN;
   if (n == 0) return GDN_OK;
+  uint32_t* status = device_status_ptr();
+  if (!status) return GDN_ERR_CUDA;
   const int64_t code_rec = (int64_t)HV * D * D / 2;
   const int64_t scale_rec = (int64_t)HV * D * D / 16;
   const int64_t vecs = (code_rec + scale_rec) / 16;
@@ -76,10 +80,10 @@ int pool_copy(bool gather, const uint8_t* sc, const uint8_t* ss, const float* sg
   dim3 grid((unsigned)gx, (unsigned)n);
   if (gather)
     pool_copy_kernel<true><<<grid, kThreads, 0, stream>>>(sc, ss, sg, dc, ds, dg, slot_idx, num_slots, HV, code_rec,
-                                                          scale_rec, n);
+                                                          scale_rec, n, status);
   else
     pool_copy_kernel<false><<<grid, kThreads, 0, stream>>>(sc, ss, sg, dc, ds, dg, slot_idx, num_slots, HV,
-                                                           code_rec, scale_rec, n);
+                                                           code_rec, scale_rec, n, status);
   return launch_status();
 }
 

@@ -47,6 +47,34 @@ int sm_count() {
   return g_sm_count[dev];
 }
 
+namespace {
+struct SmemOptIn {
+  const void* func;
+  int dev;
+  int bytes;
+};
+constexpr int kMaxOptIns = 256;
+SmemOptIn g_optins[kMaxOptIns];
+int g_num_optins = 0;
+}  // namespace
+
+int allow_dynamic_smem(const void* func, int bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_CUDA;
+  // The table is searched and extended under the lock, and the attribute is
+  // set while holding it, so concurrent first calls set it once and every
+  // caller returns only after it is in place.
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (int i = 0; i < g_num_optins; ++i)
+    if (g_optins[i].func == func && g_optins[i].dev == dev && g_optins[i].bytes >= bytes) return GDN_OK;
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return GDN_ERR_CUDA;
+  }
+  if (g_num_optins < kMaxOptIns) g_optins[g_num_optins++] = {func, dev, bytes};
+  return GDN_OK;
+}
+
 // Exercises the bounded mbarrier wait every kernel uses (common.cuh) on both
 // of its exits: a phase that completes (one arrival) and a phase that nothing
 // completes, which must give up after timeout_ns and record the timeout bit.

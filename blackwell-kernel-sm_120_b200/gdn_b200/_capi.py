@@ -22,6 +22,7 @@ GDN_ERR_CUDA = 9
 
 GDN_STATUS_WAIT_TIMEOUT = 0x1
 GDN_STATUS_BAD_SLOT = 0x2
+GDN_STATUS_BAD_SEQLENS = 0x4
 
 SCALE_REF240 = 0
 SCALE_FN448 = 1
@@ -30,7 +31,7 @@ SCALE_FN448 = 1
 EXPORTED_SYMBOLS = (
     "launch_gdn_state_update",
     "launch_gdn_ref",
-    "gdn_legacy_set_rounding",
+    "gdn_legacy_update_rounding",
     "gdn_nvfp4_quantize",
     "gdn_nvfp4_dequantize",
     "gdn_nvfp4_quantize_tiles",
@@ -41,6 +42,7 @@ EXPORTED_SYMBOLS = (
     "gdn_pool_scatter",
     "gdn_b200_device_status",
     "gdn_b200_selftest_wait",
+    "gdn_b200_selftest_codec",
     "gdn_b200_error_string",
     "gdn_b200_version",
 )
@@ -100,7 +102,8 @@ def _load() -> ctypes.CDLL:
     sig = {
         "launch_gdn_state_update": (ctypes.c_int, [_p, _p, _p, _p, _p, _p, _f32, _f32, ctypes.c_int, _p]),
         "launch_gdn_ref": (None, [_p, _p, _p, _p, _p, _f32, _f32, ctypes.c_int, _p]),
-        "gdn_legacy_set_rounding": (ctypes.c_int, [ctypes.c_int]),
+        "gdn_legacy_update_rounding": (ctypes.c_int, [_p, _p, _p, _p, _p, _p, _p, _f32, _f32, ctypes.c_int,
+                                                      ctypes.c_int, _p]),
         "gdn_nvfp4_quantize": (ctypes.c_int, [_p, _p, _p, _i64, _i32, _p]),
         "gdn_nvfp4_dequantize": (ctypes.c_int, [_p, _p, _p, _i64, _i32, _p]),
         "gdn_nvfp4_quantize_tiles": (ctypes.c_int, [_p, _i64, _i64, _p, _p, _p, _i32, _f32, _p]),
@@ -111,6 +114,7 @@ def _load() -> ctypes.CDLL:
         "gdn_pool_scatter": (ctypes.c_int, [_p, _p, _p, _i64, _i32, _i32, _p, _i32, _p, _p, _p, _p]),
         "gdn_b200_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, _p]),
         "gdn_b200_selftest_wait": (ctypes.c_int, [ctypes.c_uint32, _p, _p]),
+        "gdn_b200_selftest_codec": (ctypes.c_int, [_i32, ctypes.c_uint32, _i64, _i32, _p, _p]),
         "gdn_b200_error_string": (ctypes.c_char_p, [ctypes.c_int]),
         "gdn_b200_version": (ctypes.c_char_p, []),
     }

@@ -92,9 +92,17 @@ def nvfp4_dequantize_tiles(codes: torch.Tensor, scales: torch.Tensor, gscale: to
 
 # ---- legacy op -------------------------------------------------------------------
 
-def legacy_state_update(S_data, S_scales, k, v, alpha: float, beta: float, d: int, out=None):
+# Rounding of alpha*s + (beta*k)*v that the reference's kernel uses as compiled
+# for sm_100a; launch_gdn_state_update and launch_gdn_ref always use it.
+LEGACY_REFERENCE_ROUNDING = 1
+
+
+def legacy_state_update(S_data, S_scales, k, v, alpha: float, beta: float, d: int, out=None,
+                        rounding: int | None = None):
     """launch_gdn_state_update through the C ABI (freshly allocated outputs, as
-    the reference op does, unless `out=(data, scales)` is given)."""
+    the reference op does, unless `out=(data, scales)` is given).  `rounding`
+    (0, 1 or 2, see gdn_legacy_update_rounding) selects another rounding of
+    the update for this call only."""
     _need(S_data, torch.uint8, "S_data")
     _need(S_scales, torch.uint8, "S_scales")
     _need(k, torch.bfloat16, "k")
@@ -105,22 +113,41 @@ def legacy_state_update(S_data, S_scales, k, v, alpha: float, beta: float, d: in
     if out is None:
         out = (torch.empty(n // 2, dtype=torch.uint8, device=S_data.device),
                torch.empty(n // 16, dtype=torch.uint8, device=S_data.device))
-    rc = lib.launch_gdn_state_update(_ptr(S_data), _ptr(S_scales), _ptr(k), _ptr(v), _ptr(out[0]), _ptr(out[1]),
-                                     float(alpha), float(beta), int(d), _stream(S_data))
-    check("launch_gdn_state_update", rc)
+    if rounding is None:
+        rc = lib.launch_gdn_state_update(_ptr(S_data), _ptr(S_scales), _ptr(k), _ptr(v), _ptr(out[0]),
+                                         _ptr(out[1]), float(alpha), float(beta), int(d), _stream(S_data))
+        check("launch_gdn_state_update", rc)
+    else:
+        rc = lib.gdn_legacy_update_rounding(_ptr(S_data), _ptr(S_scales), _ptr(k), _ptr(v), _ptr(out[0]),
+                                            _ptr(out[1]), None, float(alpha), float(beta), int(d), int(rounding),
+                                            _stream(S_data))
+        check("gdn_legacy_update_rounding", rc)
     return out
 
 
-def legacy_ref_update(S_data, S_scales, k, v, alpha: float, beta: float, d: int) -> torch.Tensor:
-    """launch_gdn_ref: fp32 S' = alpha*S + beta*k v^T."""
+def legacy_ref_update(S_data, S_scales, k, v, alpha: float, beta: float, d: int,
+                      rounding: int | None = None) -> torch.Tensor:
+    """launch_gdn_ref: fp32 S' = alpha*S + beta*k v^T (or, with `rounding`,
+    gdn_legacy_update_rounding's fp32 form)."""
     out = torch.empty(d * d, dtype=torch.float32, device=S_data.device)
-    lib.launch_gdn_ref(_ptr(S_data), _ptr(S_scales), _ptr(k), _ptr(v), _ptr(out), float(alpha), float(beta),
-                       int(d), _stream(S_data))
+    if rounding is None:
+        lib.launch_gdn_ref(_ptr(S_data), _ptr(S_scales), _ptr(k), _ptr(v), _ptr(out), float(alpha), float(beta),
+                           int(d), _stream(S_data))
+    else:
+        check("gdn_legacy_update_rounding",
+              lib.gdn_legacy_update_rounding(_ptr(S_data), _ptr(S_scales), _ptr(k), _ptr(v), None, None, _ptr(out),
+                                             float(alpha), float(beta), int(d), int(rounding), _stream(S_data)))
     return out
 
 
-def legacy_set_rounding(variant: int) -> int:
-    return lib.gdn_legacy_set_rounding(int(variant))
+def codec_selftest(which: int, lo_bits: int, count: int, scale_mode: int = SCALE_REF240,
+                   device: torch.device | str = "cuda") -> torch.Tensor:
+    """gdn_b200_selftest_codec: one byte per fp32 bit pattern lo_bits + i."""
+    out = torch.empty(count, dtype=torch.uint8, device=device)
+    check("gdn_b200_selftest_codec",
+          lib.gdn_b200_selftest_codec(int(which), int(lo_bits), int(count), int(scale_mode), out.data_ptr(),
+                                      _stream(out)))
+    return out
 
 
 # ---- decode ------------------------------------------------------------------------
@@ -302,6 +329,6 @@ def default_q_scale(head_dim: int) -> float:
 
 __all__ = [
     "SCALE_REF240", "SCALE_FN448", "nvfp4_quantize", "nvfp4_dequantize", "nvfp4_quantize_tiles",
-    "nvfp4_dequantize_tiles", "legacy_state_update", "legacy_ref_update", "legacy_set_rounding", "decode",
+    "nvfp4_dequantize_tiles", "legacy_state_update", "legacy_ref_update", "LEGACY_REFERENCE_ROUNDING", "codec_selftest", "decode",
     "pool_gather", "pool_scatter", "device_status", "default_q_scale",
 ]

@@ -25,6 +25,13 @@ from . import ops
 from .pool import NVFP4StatePool
 
 
+def l2norm(x: torch.Tensor) -> torch.Tensor:
+    """x / sqrt(sum x^2 + 1e-6) per head in fp32, then bf16: vLLM/fla's l2norm
+    and the decode kernel's fused q/k normalisation."""
+    xf = x.float()
+    return (xf * torch.rsqrt((xf * xf).sum(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+
+
 def _to_pool(states_vk: torch.Tensor, scale_mode: int = 0) -> NVFP4StatePool:
     """[N, HV, V, K] dense states -> an NVFP4 pool with slots 0..N-1."""
     N, HV, V, K = states_vk.shape
@@ -46,8 +53,8 @@ def chunk_gated_delta_rule(q, k, v, g, beta, initial_state, output_final_state: 
         raise ValueError("expected packed varlen inputs of shape [1, T, H, D]")
     qs, ks, vs = q[0], k[0], v[0]
     if use_qk_l2norm_in_kernel:
-        qs = F.normalize(qs.float(), dim=-1).to(torch.bfloat16)
-        ks = F.normalize(ks.float(), dim=-1).to(torch.bfloat16)
+        qs = l2norm(qs)
+        ks = l2norm(ks)
     qs, ks, vs = (t.to(torch.bfloat16).contiguous() for t in (qs, ks, vs))
     T = qs.shape[0]
     if cu_seqlens is None:
@@ -106,4 +113,9 @@ def fused_sigmoid_gating_delta_rule_update(A_log, a, b, dt_bias, q, k, v, initia
     new = _from_pool(pool, initial_state.dtype)
     if inplace_final_state:
         initial_state[idx[valid]] = new[valid]
-    return o.unsqueeze(0), initial_state
+        return o.unsqueeze(0), initial_state
+    # vLLM's out-of-place form: a fresh [B, HV, V, K] tensor of the states
+    # after this token, row i for sequence i (padding rows zero)
+    final = torch.zeros_like(new)
+    final[valid] = new[valid]
+    return o.unsqueeze(0), final

@@ -8,7 +8,9 @@
  *     synchronisation, no host round trip (gdn_b200_device_status is the one
  *     exception and says so).  The caller owns every buffer.
  *   - Calls are stateless and safe from any host thread; ordering is per
- *     stream.  Errors are integer status codes (GDN_OK == 0).
+ *     stream.  The library's only host state is set up once per device under
+ *     a lock (the device status word's address, the SM count, the kernels'
+ *     shared-memory opt-in).  Errors are integer status codes (GDN_OK == 0).
  *   - bf16 arrays are IEEE bfloat16 (__nv_bfloat16 in C++, uint16_t bit
  *     patterns in C).
  *   - Device pointers handed to the bulk-copy (TMA) kernels must be 16-byte
@@ -95,11 +97,18 @@ GDN_API void launch_gdn_ref(const uint8_t* S_data, const uint8_t* S_scales, cons
                     const gdn_bf16_t* v, float* S_out, float alpha, float beta, int d,
                     cudaStream_t stream);
 
-/* Selects how the legacy update rounds alpha*s + (beta*k)*v:
- * 0 = fmaf(alpha, s, (beta*k)*v), 1 = fmaf(beta*k, v, alpha*s), 2 = no FMA.
- * Returns the previous setting.  The default matches the reference kernel as
- * compiled for sm_100a. */
-GDN_API int gdn_legacy_set_rounding(int variant);
+/* The legacy update with an explicit rounding of alpha*s + (beta*k)*v, chosen
+ * per call (no counterpart in the reference, whose compiler picks one):
+ * rounding 0 = fmaf(alpha, s, (beta*k)*v), 1 = fmaf(beta*k, v, alpha*s),
+ * 2 = no FMA.  launch_gdn_state_update and launch_gdn_ref always use 1, the
+ * rounding of the reference kernel as compiled for sm_100a.  With S_out_f32
+ * set it writes the fp32 update as launch_gdn_ref does (S_out_data and
+ * S_out_scales unused); otherwise the NVFP4 result as launch_gdn_state_update
+ * does.  Returns GDN_ERR_ARGS for a rounding outside 0..2. */
+GDN_API int gdn_legacy_update_rounding(const uint8_t* S_data, const uint8_t* S_scales, const gdn_bf16_t* k,
+                                       const gdn_bf16_t* v, uint8_t* S_out_data, uint8_t* S_out_scales,
+                                       float* S_out_f32, float alpha, float beta, int d, int rounding,
+                                       cudaStream_t stream);
 
 /* ---- NVFP4 codec ----------------------------------------------------------- */
 
@@ -229,13 +238,15 @@ GDN_API int gdn_prefill(const gdn_prefill_params* params, cudaStream_t stream);
 /* ---- state pool ------------------------------------------------------------ */
 
 /* Copies tiles pool[slot_idx[i]] -> dense[i] for i < n (negative slot: the
- * dense tile is zeroed).  Tile = HV heads of D x D states. */
+ * dense tile is zeroed).  Tile = HV heads of D x D states.  A slot >=
+ * num_slots is treated as padding and sets GDN_STATUS_BAD_SLOT. */
 GDN_API int gdn_pool_gather(const uint8_t* pool_codes, const uint8_t* pool_scales, const float* pool_gscale,
                     int64_t num_slots, int32_t num_v_heads, int32_t head_dim,
                     const int32_t* slot_idx, int32_t n, uint8_t* dense_codes,
                     uint8_t* dense_scales, float* dense_gscale, cudaStream_t stream);
 
-/* Copies dense[i] -> pool[slot_idx[i]] (negative slot: skipped). */
+/* Copies dense[i] -> pool[slot_idx[i]] (negative slot: skipped; a slot >=
+ * num_slots is skipped and sets GDN_STATUS_BAD_SLOT). */
 GDN_API int gdn_pool_scatter(const uint8_t* dense_codes, const uint8_t* dense_scales,
                      const float* dense_gscale, int64_t num_slots, int32_t num_v_heads,
                      int32_t head_dim, const int32_t* slot_idx, int32_t n, uint8_t* pool_codes,
@@ -254,6 +265,18 @@ GDN_API int gdn_b200_device_status(uint32_t* status_out, int clear, cudaStream_t
  * GDN_STATUS_WAIT_TIMEOUT.  result: device int32[3] = {first wait succeeded,
  * second wait succeeded, microseconds the second waited}.  Stream-ordered. */
 GDN_API int gdn_b200_selftest_wait(uint32_t timeout_us, int32_t* result, cudaStream_t stream);
+
+/* Self-test of the device codec (no counterpart in the reference): runs a
+ * production encoder over the fp32 values whose bit patterns are lo_bits,
+ * lo_bits + 1, ..., lo_bits + count - 1 (lo_bits + count <= 2^32) and writes
+ * one byte per value to the device array out [count]:
+ *   which 0: the block scale byte the requantisers write for a block whose
+ *            max |y| is that value (finite, >= 0), in scale_mode;
+ *   which 1: the E2M1 nibble of that value at inverse scale 1.
+ * The tests compare every finite input against the reference's encoders.
+ * Stream-ordered. */
+GDN_API int gdn_b200_selftest_codec(int32_t which, uint32_t lo_bits, int64_t count, int32_t scale_mode,
+                                    uint8_t* out, cudaStream_t stream);
 
 GDN_API const char* gdn_b200_error_string(int code);
 GDN_API const char* gdn_b200_version(void);

@@ -64,6 +64,8 @@ _ORACLE_SIGS = {
                                    _i64, _p, _i64, _f64]),
     "orc_sqnr_db": (_f64, [_p, _p, _i64]),
     "orc_scale_encode_sweep": (None, [_u32, _u32, ctypes.c_uint64, ctypes.c_int, _p]),
+    "orc_block_scale_sweep": (None, [_u32, ctypes.c_uint64, ctypes.c_int, _p]),
+    "orc_e2m1_sweep": (None, [_u32, ctypes.c_uint64, _p]),
     "orc_libc_srand": (None, [ctypes.c_uint]),
     "orc_libc_fill_uniform": (None, [_p, _i64, _f32, _f32]),
 }
@@ -75,6 +77,8 @@ _REF_SIGS = {
     "ref_decode_ue4m3": (_f32, [_u32]),
     "ref_encode_ue4m3": (_u32, [_f32]),
     "ref_encode_ue4m3_sweep": (None, [_u32, _u32, ctypes.c_uint64, _p]),
+    "ref_block_scale_sweep": (None, [_u32, ctypes.c_uint64, _p]),
+    "ref_e2m1_sweep": (None, [_u32, ctypes.c_uint64, _p]),
     "launch_gdn_state_update": (ctypes.c_int, [_p, _p, _p, _p, _p, _p, _f32, _f32, ctypes.c_int, _p]),
     "launch_gdn_ref": (None, [_p, _p, _p, _p, _p, _f32, _f32, ctypes.c_int, _p]),
 }
@@ -280,6 +284,46 @@ def ref_scale_encode_sweep(lo: int, stride: int, count: int) -> np.ndarray:
     out = np.zeros(count, np.uint8)
     ref().ref_encode_ue4m3_sweep(lo, stride, count, _ptr(out))
     return out
+
+
+def _threaded_sweep(fn, lo: int, count: int, threads: int | None, *extra) -> np.ndarray:
+    """Runs fn(lo_i, count_i, *extra, out_i) on `threads` slices of the range
+    in parallel (ctypes releases the GIL during the call)."""
+    import concurrent.futures
+    import os
+    out = np.zeros(count, np.uint8)
+    threads = threads or max(1, len(os.sched_getaffinity(0)))
+    step = -(-count // threads)
+    step += (-step) % 15  # keep the reference's 15-value groups whole
+    jobs = []
+    with concurrent.futures.ThreadPoolExecutor(threads) as ex:
+        for s0 in range(0, count, step):
+            n = min(step, count - s0)
+            view = out[s0:s0 + n]
+            jobs.append(ex.submit(fn, lo + s0, n, *extra, view.ctypes.data))
+        for j in jobs:
+            j.result()
+    return out
+
+
+def block_scale_sweep(lo: int, count: int, mode: int = 0, threads: int | None = None) -> np.ndarray:
+    """Oracle block scale byte of every block max with bit pattern lo + i."""
+    return _threaded_sweep(lambda a, n, m, o: oracle().orc_block_scale_sweep(a, n, m, o), lo, count, threads, mode)
+
+
+def e2m1_sweep(lo: int, count: int, threads: int | None = None) -> np.ndarray:
+    """Oracle E2M1 nibble of every value with bit pattern lo + i."""
+    return _threaded_sweep(lambda a, n, o: oracle().orc_e2m1_sweep(a, n, o), lo, count, threads)
+
+
+def ref_block_scale_sweep(lo: int, count: int, threads: int | None = None) -> np.ndarray:
+    """The reference's block scale byte (amax/6 through its encoder), bit patterns lo + i."""
+    return _threaded_sweep(lambda a, n, o: ref().ref_block_scale_sweep(a, n, o), lo, count, threads)
+
+
+def ref_e2m1_sweep(lo: int, count: int, threads: int | None = None) -> np.ndarray:
+    """The reference quantiser's E2M1 nibble of every value (|v| <= 6) with bit pattern lo + i."""
+    return _threaded_sweep(lambda a, n, o: ref().ref_e2m1_sweep(a, n, o), lo, count, threads)
 
 
 # ---- helpers shared by tests and the bench ----------------------------------------

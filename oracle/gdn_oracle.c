@@ -441,6 +441,22 @@ ORC_API void orc_scale_encode_sweep(uint32_t lo, uint32_t stride, uint64_t count
   }
 }
 
+/* Block scale byte for every block max |y| with bit pattern lo + i: the
+ * reference quantiser's local scale amax/6 (1.0 for amax 0) through the scale
+ * encoder (gdn_state_update_ref.cu:105-108). */
+ORC_API void orc_block_scale_sweep(uint32_t lo, uint64_t count, int mode, uint8_t* out) {
+  for (uint64_t i = 0; i < count; ++i) {
+    const float amax = f32_from_bits(lo + (uint32_t)i);
+    const float local = (amax > 0.0f) ? (amax / 6.0f) : 1.0f;
+    out[i] = (uint8_t)orc_scale_encode(local, mode);
+  }
+}
+
+/* E2M1 nibble (the reference scan) of every value with bit pattern lo + i. */
+ORC_API void orc_e2m1_sweep(uint32_t lo, uint64_t count, uint8_t* out) {
+  for (uint64_t i = 0; i < count; ++i) out[i] = (uint8_t)e2m1_encode_ref(f32_from_bits(lo + (uint32_t)i));
+}
+
 /* The reference's M3 gate draws its inputs from the C library's rand() after
  * srand(42) (tests/test_gdn_correctness.cu:50-54, :101-104, :200):
  *   x = lo + (hi - lo) * ((float)rand() / (float)RAND_MAX)   in float. */

@@ -37,4 +37,37 @@ void ref_encode_ue4m3_sweep(uint32_t lo, uint32_t stride, uint64_t count, uint8_
     out[i] = sm120::intrinsics::encode_f32_to_ue4m3(f);
   }
 }
+// The reference's block scale byte for every block max |y| with bit pattern
+// lo + i: its two lines local_scale = amax > 0 ? amax / 6 : 1 and the encoder
+// call (gdn_state_update_ref.cu:105-108), the encoder being the reference's own.
+void ref_block_scale_sweep(uint32_t lo, uint64_t count, uint8_t* out) {
+  for (uint64_t i = 0; i < count; ++i) {
+    const uint32_t u = lo + (uint32_t)i;
+    float amax;
+    __builtin_memcpy(&amax, &u, 4);
+    const float local = (amax > 0.0f) ? (amax / 6.0f) : 1.0f;
+    out[i] = sm120::intrinsics::encode_f32_to_ue4m3(local);
+  }
+}
+// The reference's E2M1 nibble of every value v with bit pattern lo + i and
+// |v| <= 6, through its own nvfp4_quantise_host: each call quantises the block
+// {6, v_0, ..., v_14}, whose max is 6, so its scale decodes to exactly 1.0 and
+// element j + 1's nibble is the reference's nearest-E2M1 of v_j.
+void ref_e2m1_sweep(uint32_t lo, uint64_t count, uint8_t* out) {
+  float blk[16];
+  uint8_t codes[8], scale;
+  for (uint64_t i0 = 0; i0 < count; i0 += 15) {
+    const int n = (count - i0) < 15 ? (int)(count - i0) : 15;
+    blk[0] = 6.0f;
+    for (int j = 0; j < 15; ++j) {
+      const uint32_t u = lo + (uint32_t)(i0 + (j < n ? j : 0));
+      __builtin_memcpy(&blk[j + 1], &u, 4);
+    }
+    nvfp4_quantise_host(blk, codes, &scale, 16);
+    for (int j = 0; j < n; ++j) {
+      const int e = j + 1;
+      out[i0 + j] = (uint8_t)((codes[e / 2] >> (4 * (e & 1))) & 0xFu);
+    }
+  }
+}
 }

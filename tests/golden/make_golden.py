@@ -1,7 +1,8 @@
 """Regenerates the committed golden fixtures in tests/golden/.
 
 Run in a checkout that has the reference (bojak83318/blackwell-kernel-sm_120)
-at $GDN_REFERENCE_DIR (default /root/reference) and the oracle built
+at $GDN_REFERENCE_DIR (default: a checkout named `reference` beside this
+repository) and the oracle built
 (`make -C oracle && make -C oracle ref`):
 
     python tests/golden/make_golden.py
@@ -81,7 +82,7 @@ def edge_blocks() -> np.ndarray:
 
 
 def main() -> None:
-    ref_dir = pathlib.Path(os.environ.get("GDN_REFERENCE_DIR", "/root/reference"))
+    ref_dir = pathlib.Path(os.environ.get("GDN_REFERENCE_DIR", HERE.parents[2] / "reference"))
     tables = parse_tables(ref_dir)
     tables["source"] = "tests/unit/m1_intrinsics.hpp:22-58 of bojak83318/blackwell-kernel-sm_120"
     tables["note"] = ("E2M1 entries 6, 7, 14, 15 of the unit test decode to inf/NaN; the product decoder "

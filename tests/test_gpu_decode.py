@@ -285,3 +285,56 @@ def test_torch_op_decode_matches_c_abi(cuda):
     o2 = gdn_op.decode(x["q"][0], x["k"][0], x["v"][0], x["g"][0], x["beta"][0], slot, p2)
     assert torch.equal(o1, o2)
     assert torch.equal(p1.codes, p2.codes)
+
+
+def _twin_pools(n_slots, mode, slot, seed):
+    """Two pools with identical bytes: random states loaded into `slot`."""
+    from gdn_b200 import NVFP4StatePool, workloads
+    states = workloads.initial_states(slot.numel(), HV, D, seed=seed).cuda()
+    pools = []
+    for _ in range(2):
+        p = NVFP4StatePool.zeros(n_slots, HV, D, "cuda", scale_mode=mode)
+        p.load_fp32(states, slot)
+        pools.append(p)
+    return pools
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("B,n_slots", [(4, 8), (256, 2048)])
+def test_production_instance_writes_the_debug_instance_bytes(cuda, mode, B, n_slots):
+    """The serving kernel (no debug_y) and the instance the bit-exact tests run
+    (debug_y set) write identical codes, scales, global scales and outputs,
+    over two consecutive steps, so the bit-exactness shown on the debug
+    instance holds for the production one."""
+    from gdn_b200 import workloads
+    slot = workloads.slot_permutation(B, n_slots, seed=11 + B).cuda()
+    prod, dbg = _twin_pools(n_slots, mode, slot, seed=12)
+    x = _inputs(B, 2, seed=13)
+    for t in range(2):
+        o_p, _ = _gpu_step(prod, x, t, slot, debug=False)
+        o_d, _ = _gpu_step(dbg, x, t, slot, debug=True)
+        assert torch.equal(o_p, o_d)
+        assert torch.equal(prod.codes, dbg.codes)
+        assert torch.equal(prod.scales, dbg.scales)
+        assert torch.equal(prod.gscale.view(torch.int32), dbg.gscale.view(torch.int32))
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_fused_norm_instance_writes_the_plain_instance_pool_bytes(cuda, mode):
+    """The fused gated-norm instance changes only the output: its pool bytes
+    equal the plain (production) instance's, at batch 256 on a random map."""
+    from gdn_b200 import ops, workloads
+    B, n_slots = 256, 2048
+    slot = workloads.slot_permutation(B, n_slots, seed=21).cuda()
+    plain, normed = _twin_pools(n_slots, mode, slot, seed=22)
+    x = _inputs(B, 1, seed=23)
+    gen = torch.Generator().manual_seed(24)
+    z = torch.randn((B, HV, D), generator=gen).to(torch.bfloat16).cuda()
+    w = (1.0 + 0.1 * torch.randn(D, generator=gen)).cuda()
+    args = (x["q"][0], x["k"][0], x["v"][0], x["g"][0], x["beta"][0], slot)
+    ops.decode(*args, plain)
+    ops.decode(*args, normed, norm_weight=w, gate_z=z)
+    torch.cuda.synchronize()
+    assert torch.equal(plain.codes, normed.codes)
+    assert torch.equal(plain.scales, normed.scales)
+    assert torch.equal(plain.gscale.view(torch.int32), normed.gscale.view(torch.int32))

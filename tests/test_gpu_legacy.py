@@ -56,35 +56,49 @@ def _ref_f32(ref_lib, sd, ss, kb, vb, a, b, d):
     return out.cpu().numpy()
 
 
-def _ours(sd, ss, kb, vb, a, b, d, variant=None):
+def _ours(sd, ss, kb, vb, a, b, d, rounding=None):
     from gdn_b200 import ops
-    prev = ops.legacy_set_rounding(variant) if variant is not None else None
-    try:
-        od, os_ = ops.legacy_state_update(_dev(sd), _dev(ss), _dev(kb).view(torch.bfloat16),
-                                          _dev(vb).view(torch.bfloat16), a, b, d)
-        torch.cuda.synchronize()
-    finally:
-        if prev is not None:
-            ops.legacy_set_rounding(prev)
+    od, os_ = ops.legacy_state_update(_dev(sd), _dev(ss), _dev(kb).view(torch.bfloat16),
+                                      _dev(vb).view(torch.bfloat16), a, b, d, rounding=rounding)
+    torch.cuda.synchronize()
     return od.cpu().numpy(), os_.cpu().numpy()
 
 
 def test_default_rounding_matches_reference_binary_fp32(cuda, ref_lib, oracle_lib):
     """launch_gdn_ref: our fused kernel equals the reference's two kernels bit
-    for bit (the default rounding variant is the one its compiled line uses)."""
+    for bit.  The rounding the reference entry points use is the one its
+    compiled line uses; the per-call variants show that the comparison can
+    tell the three roundings apart."""
     from gdn_b200 import ops
     d, a, b, sd, ss, kb, vb = _m3_inputs(oracle_lib)[0]
     ref = _ref_f32(ref_lib, sd, ss, kb, vb, a, b, d)
-    matches = {}
+    args = (_dev(sd), _dev(ss), _dev(kb).view(torch.bfloat16), _dev(vb).view(torch.bfloat16), a, b, d)
+    mismatch = {}
     for var in range(3):
-        prev = ops.legacy_set_rounding(var)
-        out = ops.legacy_ref_update(_dev(sd), _dev(ss), _dev(kb).view(torch.bfloat16), _dev(vb).view(torch.bfloat16),
-                                    a, b, d).cpu().numpy()
-        ops.legacy_set_rounding(prev)
-        matches[var] = int((out.view(np.uint32) != ref.view(np.uint32)).sum())
-    default = ops.legacy_set_rounding(0)
-    ops.legacy_set_rounding(default)
-    assert matches[default] == 0, f"mismatching elements per variant: {matches} (default {default})"
+        out = ops.legacy_ref_update(*args, rounding=var).cpu().numpy()
+        mismatch[var] = int((out.view(np.uint32) != ref.view(np.uint32)).sum())
+    default = ops.legacy_ref_update(*args).cpu().numpy()
+    assert np.array_equal(default.view(np.uint32), ref.view(np.uint32))
+    assert mismatch[ops.LEGACY_REFERENCE_ROUNDING] == 0, mismatch
+    assert sum(1 for m in mismatch.values() if m == 0) == 1, f"variants indistinguishable: {mismatch}"
+
+
+def test_per_call_rounding_leaves_reference_entry_unchanged(cuda, oracle_lib):
+    """A call with another rounding changes nothing for later default calls:
+    there is no process-wide rounding state."""
+    from gdn_b200 import ops
+    d, a, b, sd, ss, kb, vb = _m3_inputs(oracle_lib)[0]
+    before = _ours(sd, ss, kb, vb, a, b, d)
+    for var in (0, 2):
+        _ours(sd, ss, kb, vb, a, b, d, rounding=var)
+    after = _ours(sd, ss, kb, vb, a, b, d)
+    for x, y in zip(before, after):
+        np.testing.assert_array_equal(x, y)
+    ref = _ours(sd, ss, kb, vb, a, b, d, rounding=ops.LEGACY_REFERENCE_ROUNDING)
+    for x, y in zip(before, ref):
+        np.testing.assert_array_equal(x, y)
+    with pytest.raises(Exception):
+        _ours(sd, ss, kb, vb, a, b, d, rounding=3)
 
 
 @pytest.mark.parametrize("case", range(3))

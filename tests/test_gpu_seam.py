@@ -109,3 +109,35 @@ def test_seam_decode_in_place(cuda):
             assert torch.equal(ssm[s], new[i])
     for s in (1, 3, 5, 6, 8):
         assert torch.equal(ssm[s], before[s])
+
+
+def test_seam_decode_out_of_place(cuda):
+    """inplace_final_state=False: the cache is left alone and the states after
+    the token come back in a fresh [B, HV, V, K] tensor (row i = sequence i,
+    padding rows zero), as vLLM's own function returns them."""
+    from gdn_b200 import vllm_seam, workloads
+    B, slots = 5, 8
+    x = workloads.decode_steps(B, 1, HK, HV, D, seed=31, device="cuda")
+    gen = torch.Generator(device="cpu").manual_seed(7)
+    A_log, dt_bias = torch.randn(HV, generator=gen).cuda(), torch.randn(HV, generator=gen).cuda()
+    a, b = torch.randn(B, HV, generator=gen).cuda(), torch.randn(B, HV, generator=gen).cuda()
+    ssm = workloads.initial_states(slots, HV, D, seed=8).cuda().transpose(-1, -2).contiguous()
+    idx = torch.tensor([3, -1, 0, 7, 5], dtype=torch.int32, device="cuda")
+    args = (A_log, a, b, dt_bias, x["q"][0].unsqueeze(0), x["k"][0].unsqueeze(0), x["v"][0].unsqueeze(0))
+    cache = ssm.clone()
+    o1, final = vllm_seam.fused_sigmoid_gating_delta_rule_update(*args, cache, inplace_final_state=False,
+                                                                 ssm_state_indices=idx)
+    torch.cuda.synchronize()
+    assert torch.equal(cache, ssm)
+    assert final.shape == (B, HV, D, D) and final is not cache
+    in_place = ssm.clone()
+    o2, st = vllm_seam.fused_sigmoid_gating_delta_rule_update(*args, in_place, inplace_final_state=True,
+                                                              ssm_state_indices=idx)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2)
+    for i, s in enumerate(idx.tolist()):
+        if s >= 0:
+            assert torch.equal(final[i], st[s])
+            assert not torch.equal(final[i], ssm[s])
+        else:
+            assert int(final[i].count_nonzero()) == 0

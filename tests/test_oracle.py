@@ -61,6 +61,37 @@ def test_scale_encode_sweep_matches_compiled_reference(ref_lib):
     np.testing.assert_array_equal(a, b)
 
 
+# Bit patterns of the finite non-negative floats, and of |v| <= 6.
+FINITE_POS_END = 0x7F800000          # first non-finite pattern
+SIX_BITS = 0x40C00000                # 6.0f
+EIGHT_BITS = 0x41000000              # 8.0f
+
+
+def test_block_scale_exhaustive_matches_compiled_reference(ref_lib):
+    """Every finite block max |y| >= 0: the oracle's block scale byte equals the
+    reference's (amax/6 through its own encoder), all 2^31 - 2^23 inputs."""
+    chunk = 1 << 27
+    for lo in range(0, FINITE_POS_END, chunk):
+        n = min(chunk, FINITE_POS_END - lo)
+        a = ref_lib.block_scale_sweep(lo, n, 0)
+        b = ref_lib.ref_block_scale_sweep(lo, n)
+        bad = np.nonzero(a != b)[0]
+        assert bad.size == 0, [(hex(lo + int(i)), int(a[i]), int(b[i])) for i in bad[:8]]
+
+
+@pytest.mark.parametrize("sign", [0, 0x80000000])
+def test_e2m1_exhaustive_matches_compiled_reference(ref_lib, sign):
+    """Every float with |v| <= 6 of either sign (-0 included): the oracle's
+    nearest-E2M1 scan equals the reference quantiser's, bit for bit."""
+    chunk = 1 << 27
+    for lo in range(0, SIX_BITS + 1, chunk):
+        n = min(chunk, SIX_BITS + 1 - lo)
+        a = ref_lib.e2m1_sweep(sign + lo, n)
+        b = ref_lib.ref_e2m1_sweep(sign + lo, n)
+        bad = np.nonzero(a != b)[0]
+        assert bad.size == 0, [(hex(sign + lo + int(i)), int(a[i]), int(b[i])) for i in bad[:8]]
+
+
 def test_quantise_matches_compiled_reference_random(ref_lib):
     rng = np.random.default_rng(7)
     for scale in (1e-6, 0.02, 1.0, 4.0, 300.0, 1e8):
