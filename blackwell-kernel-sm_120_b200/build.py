@@ -8,6 +8,8 @@ Outputs (git-ignored, carried to GPU hosts with the tree):
   lib/libgdn_sm120_op.so  torch custom ops in the reference's `gdn_sm120`
                           namespace (src/ops/gdn_op.cu:103-110 of the reference),
                           linked against libgdn_b200.so
+  lib/libgdn_sm120_plugin.so  the TensorRT-LLM plugin face (include/gdn_trt_plugin.h)
+                          over the C ABI, linked against libgdn_b200.so
 
 nvcc cross-compiles for sm_100a without a GPU.  Objects are rebuilt only when a
 source or header is newer than the object.
@@ -115,6 +117,22 @@ def build_torch_op(verbose: bool = False) -> pathlib.Path | None:
     return so
 
 
+def build_plugin(verbose: bool = False) -> pathlib.Path:
+    """libgdn_sm120_plugin.so: the plugin class of include/gdn_trt_plugin.h and
+    its C entry points; needs no TensorRT."""
+    src = CSRC / "plugin" / "gdn_trt_plugin.cpp"
+    so = LIB / "libgdn_sm120_plugin.so"
+    capi = LIB / "libgdn_b200.so"
+    if not _stale(so, [src, capi, *_headers()]):
+        return so
+    cuda_lib = pathlib.Path("/usr/local/cuda/lib64")
+    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", "-Wall", f"-I{INCLUDE}",
+           "-I/usr/local/cuda/include", src, "-o", so, f"-L{LIB}", "-lgdn_b200", f"-L{cuda_lib}", "-lcudart",
+           "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{cuda_lib}"]
+    _run(cmd, verbose)
+    return so
+
+
 def reference_dir() -> pathlib.Path:
     """The reference checkout: $GDN_REFERENCE_DIR, else a checkout named
     `reference` beside this repository."""
@@ -140,6 +158,7 @@ def main() -> None:
     ap.add_argument("--ptxas", action="store_true", help="print ptxas register/smem usage")
     args = ap.parse_args()
     build_capi(args.verbose, args.ptxas)
+    build_plugin(args.verbose)
     if not args.no_torch:
         build_torch_op(args.verbose)
     if args.oracle:

@@ -118,6 +118,25 @@ inline int launch_status() {
 // SM count of the current device (cached per device).
 int sm_count();
 
+// Byte strides between consecutive (slot, head) tiles of a state pool's
+// codes, scales and global scales (128 x 128 tiles).  tile_stride 0: three
+// dense arrays (8192, 1024 and 4 bytes per tile).  Otherwise the record
+// layout, every array advancing by tile_stride: a multiple of 16 of at least
+// 9220 bytes, with the three pointers 16-, 16- and 4-byte aligned.  False
+// when the stride or the alignment is not usable.
+inline bool pool_strides(int64_t tile_stride, const void* codes, const void* scales, const void* gscale,
+                         int64_t* code_stride, int64_t* scale_stride, int64_t* gs_stride) {
+  if (tile_stride == 0) {
+    *code_stride = 8192;
+    *scale_stride = 1024;
+    *gs_stride = 4;
+  } else {
+    if (tile_stride < 9220 || tile_stride % 16) return false;
+    *code_stride = *scale_stride = *gs_stride = tile_stride;
+  }
+  return aligned16(codes) && aligned16(scales) && (reinterpret_cast<uintptr_t>(gscale) & 3u) == 0;
+}
+
 // Raises `func`'s dynamic shared-memory limit to `bytes` on the current
 // device, once per (kernel, device); safe to call from any host thread.
 // Returns GDN_OK or GDN_ERR_CUDA.

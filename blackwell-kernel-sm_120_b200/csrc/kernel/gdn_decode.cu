@@ -5,24 +5,31 @@
 // in the pool slot named by slot_idx:
 //   alpha = exp(g), S_a = alpha S, u = S_a^T k, w = beta (v - u),
 //   S' = S_a + k w^T, o = q_scale S'^T q = q_scale (S_a^T q + (k.q) w),
-// then S' is requantised in place with a fresh global scale
-// gs' = amax(S') / gden and the reference block quantiser
-// (src/kernel/gdn_state_update_ref.cu:93-141) applied to y = S' / gs'.
+// then S' is requantised in place with a fresh power-of-two-adjusted global
+// scale and the reference block quantiser (src/kernel/gdn_state_update_ref.cu:93-141)
+// applied to y = S' / gs'.
 // The reference has no counterpart of this step (its only update is
 // S' = alpha S + beta k v^T, gdn_state_update_ref.cu:51-67); the recurrence is
 // the gated delta rule (Yang, Kautz & Hatamizadeh, ICLR 2025).
 //
 // The decode and the rank-1 update run on the tensor cores.  With
-// c = alpha gs and S_dq = e2m1 * block scale (so S = gs S_dq):
-//   MMA1'   D1' = I * S_dq^T          block-scaled E2M1 MMA against an identity
+// S_dq = e2m1 * block scale (so S = gs S_dq), an identity of E2M1 0.5 at
+// scale 2^-6 (so that the decoded tile is 2^-7 S_dq) and c = 2^7 alpha gs:
+//   MMA1'   D1' = I * S_dq^T          block-scaled E2M1 MMA against the identity
 //                                     (lane = column j)
 //   SIMT    [u p] / c = D1' [k q]     each w thread reduces half a row of D1'
 //   MMA1    D1  = S_dq * I            the tile again, lane = row i (double-buffered)
 //   MMA_r1  D1 += k (w / c)^T         tf32 rank-1 update, w / c split hi + lo
-// so S' = c D1 and the requantiser reads y = D1 * (c / gs') straight from
-// TMEM, in two passes (block maxima, then quantisation) so that a thread never
-// holds more than 32 values.  The codes arrive by one 2-D TMA copy with 64-byte
-// swizzle that both decode MMAs read in place.
+// so S' = c D1.  The new global scale is gs' = c 2^-k with k >= 0 the
+// largest integer for which max |D1| 2^k <= gden, and the quantiser input is
+// y = D1 2^k.  Scaling by 2^k is exact, so each block's E2M1 codes follow from
+// D1 and the block's own maximum alone (tile_requant.cuh); the identity's
+// 2^-7 keeps max |D1| below gden, and so k >= 0, unless the rank-1 term is
+// more than ~127x the decayed state (then an exact path runs).  The
+// requantiser reads D1 straight from TMEM in two passes (block maxima, then
+// codes) so that a thread never holds more than 32 values.  The codes arrive
+// by one 2-D TMA copy with 64-byte swizzle that both decode MMAs read in
+// place.
 //
 // Warp roles (one CTA per SM, 27 warps):
 //   warp 25     producer: walks the CTA's tiles, loads the per-tile scalars
@@ -50,7 +57,6 @@ namespace gdn {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kQWarps = 16;  // two groups of 8
 constexpr int kWWarp0 = 16;  // 8 w warps
 constexpr int kMmaWarp = 24;
 constexpr int kProdWarp = 25;
@@ -63,6 +69,8 @@ constexpr uint32_t kScaleBytes = kD * kD / 16;  // 1024
 constexpr uint32_t kVecBytes = kD * 2;          // 256
 constexpr uint32_t kStageTx = kCodeBytes + kScaleBytes + 3 * kVecBytes;
 constexpr float kDropBelow = 1e-30f;            // alpha * gs below this: the decayed state is zero
+constexpr float kIdentInv = 128.0f;             // 1 / (the identity's value 0.5 x its scale 2^-6)
+constexpr int kMaxShift = 100;                  // the fast requantiser path takes 0 <= k <= kMaxShift
 
 // Named hardware barriers (0 is __syncthreads)
 constexpr int kBarQ0 = 1, kBarQ1 = 3, kBarW = 2;
@@ -73,12 +81,12 @@ constexpr uint32_t kColD1 = 0;     // 2 x 128: D1 (lane i), one per requantiser 
 constexpr uint32_t kColD1t = 256;  // 128: D1' (lane j)
 constexpr uint32_t kColSF = 384;   // 3 x 8: the tile's scale factors (tile n uses n % 3: the
                                    // slot is rewritten only after tile n - 3's MMA1 is known complete)
-constexpr uint32_t kColOne = 408;  // 8: unit scale factors of the identity
+constexpr uint32_t kColOne = 408;  // 8: the identity's scale factors (UE4M3 2^-6)
 
 struct TileMeta {
   int64_t pt;       // slot * HV + h
   int32_t b, h;
-  float c;          // alpha * gs (1 when the decayed state is dropped)
+  float c;          // 2^7 alpha gs, S' = c D1 (1 when the decayed state is dropped)
   float inv_c;
   float beta;
   float kq;         // k . q
@@ -100,14 +108,15 @@ struct __align__(1024) Stage {
 
 struct __align__(1024) DecodeSmem {
   Stage st[kStages];
-  uint8_t ident[kCodeBytes];  // identity, no-swizzle K-major: byte b of row r at (b % 16) + 16 r + 2048 (b / 16)
-  uint8_t sf_one[kScaleBytes];
+  uint8_t ident[kCodeBytes];  // identity (E2M1 0.5), no-swizzle K-major: byte b of row r at (b % 16) + 16 r + 2048 (b / 16)
+  uint8_t sf_one[kScaleBytes];  // the identity's scale factors, UE4M3 2^-6
   uint8_t bw[2][kD * 8 * 4];    // [128][8] fp32 K-major: columns 0, 1 = hi, lo of w / c
   float2 red[kD];               // partial [u p] / c of the second half of each row of D1'
   TileMeta ring[kRing];         // metadata of valid tile n at n % kRing
   uint32_t amax_bits[2][2];     // per group, per tile parity: tile max |D1| as float bits
   float nrm[2][4];              // fused norm: per tile parity, per output warp, sum of x^2
   float inv_tab[256];
+  uint32_t rtab[8];             // scale_inv_w's reciprocal significands
   uint64_t full[kStages], ready[kStages], empty[kStages];
   uint64_t bar_t, bar_tfree, bar_w[2], bar_d[2], bar_q[2], bar_fin;
   uint32_t tmem_base;
@@ -140,6 +149,7 @@ struct DecodeArgs {
   uint8_t* pool_codes;
   uint8_t* pool_scales;
   float* pool_gs;
+  int64_t code_stride, scale_stride, gs_stride;  // bytes between consecutive (slot, head) tiles
   __nv_bfloat16* out;
   float q_scale, gden;
   float* debug_y;
@@ -158,6 +168,11 @@ struct DecodeArgs {
   float norm_eps;
   int32_t norm_act;
 };
+
+// The global scale of pool tile pt (slot * HV + head).
+__device__ __forceinline__ float* gs_at(const DecodeArgs& a, int64_t pt) {
+  return reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.pool_gs) + pt * a.gs_stride);
+}
 
 // softplus(x) = log(1 + exp(x)), the identity above 20 (torch.nn.functional.softplus, beta 1).
 __device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
@@ -197,14 +212,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---- once per CTA: tables, constant operands, barriers, TMEM ----
   if (tid < 256) sm.inv_tab[tid] = scale_inverse(scale_decode((uint32_t)tid, kMode));
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (tid == i) sm.rtab[i] = scale_inv_w_entry(i);
   for (int e = tid; e < (int)kCodeBytes; e += kThreads) {
     const int r = e >> 6, byte = e & 63;
     uint8_t val = 0;
-    if (2 * byte == r) val = 0x02;      // E2M1 1.0 in the low nibble (k = 2 byte)
-    if (2 * byte + 1 == r) val = 0x20;  // ... or the high nibble (k = 2 byte + 1)
+    if (2 * byte == r) val = 0x01;      // E2M1 0.5 in the low nibble (k = 2 byte)
+    if (2 * byte + 1 == r) val = 0x10;  // ... or the high nibble (k = 2 byte + 1)
     sm.ident[canon(r, byte)] = val;
   }
-  if (tid < 256) reinterpret_cast<uint32_t*>(sm.sf_one)[tid] = 0x38383838u;  // UE4M3 1.0
+  if (tid < 256) reinterpret_cast<uint32_t*>(sm.sf_one)[tid] = 0x08080808u;  // UE4M3 2^-6
   for (int e = tid; e < 2 * kD * 8; e += kThreads) reinterpret_cast<float*>(sm.bw)[e] = 0.0f;
   for (int e = tid; e < kStages * kD * 8; e += kThreads)
     reinterpret_cast<float*>(sm.st[e / (kD * 8)].ak)[e % (kD * 8)] = 0.0f;
@@ -290,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           gv = r.x0;
           bv = r.x1;
         }
-        q.c = expf(gv) * __ldg(a.pool_gs + q.pt);
+        q.c = expf(gv) * __ldg(gs_at(a, q.pt));
         q.beta = bv;
       }
       return q;
@@ -326,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             m.b = b;
             m.h = h;
             m.drop = (c >= 0.0f && c < kDropBelow) ? 1 : 0;
-            m.c = m.drop ? 1.0f : c;
+            m.c = m.drop ? 1.0f : c * kIdentInv;
             m.inv_c = 1.0f / m.c;
             m.beta = beta;
             m.end = 0;
@@ -334,11 +352,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint64_t* bar = &sm.full[s];
             mbar_arrive_expect_tx(bar, kStageTx + (kNorm && a.gate_z ? kVecBytes : 0u));  // also publishes the metadata
             asm volatile(
-                "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
-                "%3}], [%4];" ::"r"(smem_u32(st.codes)),
-                "l"(&tm_codes), "r"(0), "r"((int32_t)(pt * kD)), "r"(smem_u32(bar))
+                "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+                "%3, %4}], [%5];" ::"r"(smem_u32(st.codes)),
+                "l"(&tm_codes), "r"(0), "r"(0), "r"((int32_t)pt), "r"(smem_u32(bar))
                 : "memory");
-            bulk_g2s(st.scales, a.pool_scales + pt * kScaleBytes, kScaleBytes, bar);
+            bulk_g2s(st.scales, a.pool_scales + pt * a.scale_stride, kScaleBytes, bar);
             bulk_g2s(st.q, a.q + b * a.q_stride + (int64_t)hk * kD, kVecBytes, bar);
             bulk_g2s(st.k, a.k + b * a.k_stride + (int64_t)hk * kD, kVecBytes, bar);
             bulk_g2s(st.v, a.v + b * a.v_stride + (int64_t)h * kD, kVecBytes, bar);
@@ -600,6 +618,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
     const int bar_id = grp ? kBarQ1 : kBarQ0;
     const int lead = 256 * grp;                   // the group's first thread
+    const uint32_t gden_bits = __float_as_uint(a.gden);
+    constexpr uint32_t kSat = kMode ? 0x7Eu : 0x77u;
     for (int l = 0;; ++l) {
       const int n = 2 * l + grp;
       // one thread waits; the others sleep on the group's hardware barrier
@@ -610,9 +630,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (m.end) break;
       tc::fence_after_sync();
       const uint32_t ta = T + lane_base + kColD1 + 128 * grp + 64 * half;
-      // pass 1: block maxima of this thread's 64 values, columns 32-63 first; columns
-      // 0-31 stay in registers for pass 2
+      // pass 1: block maxima of this thread's 64 values, columns 32-63 first (columns
+      // 0-31 stay in registers for pass 2), and each block's provisional scale
       float am[4];
+      uint32_t ws[4];
       float tmax = 0.0f;
       float2 x0[16];
       {
@@ -635,19 +656,33 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
       if (lane == 0) atomicMax(&sm.amax_bits[grp][l & 1], __float_as_uint(tmax));
+#pragma unroll
+      for (int b = 0; b < 4; ++b) ws[b] = scale_w(am[b]);
       named_bar(bar_id, 256);
-      // S' = c D1: gs' = amax(S') / gden; y = D1 (c / gs'), computed by every thread (no second barrier)
-      const float amax_s = m.c * __uint_as_float(sm.amax_bits[grp][l & 1]);
-      const float gs_new = (amax_s > 0.0f) ? __fdiv_rn(amax_s, a.gden) : 1.0f;
-      const float mult = __fmul_rn(m.c, __frcp_rn(gs_new));
+      // A = max |D1| over the tile (NaN ignored); gs' = c 2^-k, y = D1 2^k
+      const uint32_t ab = sm.amax_bits[grp][l & 1];
       if (tid == lead) sm.amax_bits[grp][(l + 1) & 1] = 0u;  // the next tile's slot: every thread of the
                                                              // group read it (tile l - 1) before the barrier above
-      // pass 2: quantise, one 16-value block at a time
-      uint8_t* codes = a.pool_codes + m.pt * kCodeBytes + row * 64 + 32 * half;
+      int k = pow2_headroom(ab, gden_bits);
+      const bool fast = ab >= 0x00800000u && ab < 0x7F800000u && k >= 0 && k <= kMaxShift;
+      float mult, gs_new;
+      if (ab != 0u && ab < 0x7F800000u) {  // finite A > 0
+        k = k < -126 ? -126 : (k > 126 ? 126 : k);
+        mult = exp2i(k);
+        gs_new = m.c * exp2i(-k);
+      } else if (ab == 0u) {  // an all-zero tile: gs' = 1, y = S'
+        mult = m.c;
+        gs_new = 1.0f;
+      } else {  // an infinite value: gs' = inf, y = D1 * 0
+        mult = 0.0f;
+        gs_new = __uint_as_float(0x7F800000u);
+      }
+      // pass 2: codes, one pair of 16-value blocks per TMEM load and per 16-byte store
+      uint8_t* codes = a.pool_codes + m.pt * a.code_stride + row * 64 + 32 * half;
       float* dbg = kDebug ? a.debug_y + (((int64_t)m.b * a.HV + m.h) * kD + row) * kD + 64 * half : nullptr;
       uint32_t scw = 0;
 #pragma unroll
-      for (int bp = 0; bp < 2; ++bp) {  // two blocks per TMEM load and per 16-byte store
+      for (int bp = 0; bp < 2; ++bp) {
         float2 x[16];
         if (bp == 0) {
 #pragma unroll
@@ -660,14 +695,48 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.bar_q[grp]);
         }
-        const float a2[2] = {am[2 * bp], am[2 * bp + 1]};
-        uint32_t words[4], sc2;
-        requant_blocks<kMode, 2>(x, a2, mult, sm.inv_tab, words, sc2, kDebug ? dbg + 32 * bp : nullptr);
+        uint32_t words[4];
+        if (fast) {
+#pragma unroll
+          for (int b = 0; b < 2; ++b) {
+            const int bi = 2 * bp + b;
+            const uint32_t fin = ws[bi] + 8u * (uint32_t)k - 960u;
+            uint32_t sc;
+            if (fin - 8u <= kSat - 8u) {
+              // a normal, unclamped scale byte: RN(y inv) = RN(D1 scale_inv_w)
+              const float inv0 = scale_inv_w(ws[bi], sm.rtab);
+              const float2 inv2 = make_float2(inv0, inv0);
+              words[2 * b] = e2m1_encode8(x + 8 * b, inv2);
+              words[2 * b + 1] = e2m1_encode8(x + 8 * b + 4, inv2);
+              sc = fin;
+            } else {
+              // a zero, subnormal-scale, saturated or NaN block: the exact path on y = D1 2^k
+              const float a1[1] = {am[bi]};
+              uint32_t w2[2];
+              requant_blocks<kMode, 1>(*reinterpret_cast<const float2(*)[8]>(x + 8 * b), a1, mult, sm.inv_tab, w2,
+                                       sc, nullptr);
+              words[2 * b] = w2[0];
+              words[2 * b + 1] = w2[1];
+            }
+            scw |= sc << (8 * bi);
+          }
+        } else {
+          const float a2[2] = {am[2 * bp], am[2 * bp + 1]};
+          uint32_t sc2;
+          requant_blocks<kMode, 2>(x, a2, mult, sm.inv_tab, words, sc2, nullptr);
+          scw |= sc2 << (16 * bp);
+        }
         *reinterpret_cast<uint4*>(codes + 16 * bp) = make_uint4(words[0], words[1], words[2], words[3]);
-        scw |= sc2 << (16 * bp);
+        if (kDebug) {
+          float4* dy = reinterpret_cast<float4*>(dbg + 32 * bp);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            dy[e] = make_float4(__fmul_rn(x[2 * e].x, mult), __fmul_rn(x[2 * e].y, mult),
+                                __fmul_rn(x[2 * e + 1].x, mult), __fmul_rn(x[2 * e + 1].y, mult));
+        }
       }
-      *reinterpret_cast<uint32_t*>(a.pool_scales + m.pt * kScaleBytes + row * 8 + 4 * half) = scw;
-      if (tid == lead) a.pool_gs[m.pt] = gs_new;
+      *reinterpret_cast<uint32_t*>(a.pool_scales + m.pt * a.scale_stride + row * 8 + 4 * half) = scw;
+      if (tid == lead) *gs_at(a, m.pt) = gs_new;
     }
   }
 
@@ -734,8 +803,11 @@ extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
   if (a.q_stride < (int64_t)p->num_k_heads * kD || a.k_stride < (int64_t)p->num_k_heads * kD ||
       a.v_stride < (int64_t)p->num_v_heads * kD)
     return GDN_ERR_ARGS;
-  // The codes are addressed as rows of a 2-D tensor map (int32 row coordinate).
-  if (a.ntiles > INT32_MAX || p->num_slots * (int64_t)p->num_v_heads * kD > INT32_MAX) return GDN_ERR_UNSUPPORTED;
+  // The codes are addressed as tiles of a 3-D tensor map (int32 tile coordinate).
+  if (a.ntiles > INT32_MAX || p->num_slots * (int64_t)p->num_v_heads > INT32_MAX) return GDN_ERR_UNSUPPORTED;
+  if (!pool_strides(p->pool_tile_stride, p->pool_codes, p->pool_scales, p->pool_gscale, &a.code_stride,
+                    &a.scale_stride, &a.gs_stride))
+    return GDN_ERR_ALIGN;
   a.g = p->g;
   a.beta = p->beta;
   a.slot_idx = p->slot_idx;
@@ -773,12 +845,13 @@ extern "C" int gdn_decode(const gdn_decode_params* p, cudaStream_t stream) {
   {
     const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
     if (!enc) return GDN_ERR_CUDA;
-    const int64_t rows = p->num_slots > 0 ? p->num_slots * (int64_t)p->num_v_heads * kD : kD;
-    const cuuint64_t dims[2] = {64, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {64};
-    const cuuint32_t box[2] = {64, kD};
-    const cuuint32_t estr[2] = {1, 1};
-    if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p->pool_codes, dims, strides, box, estr,
+    // [tiles][128 rows][64 bytes]: one box is one tile's codes, whatever the tile stride
+    const int64_t tiles = p->num_slots > 0 ? p->num_slots * (int64_t)p->num_v_heads : 1;
+    const cuuint64_t dims[3] = {64, (cuuint64_t)kD, (cuuint64_t)tiles};
+    const cuuint64_t strides[2] = {64, (cuuint64_t)a.code_stride};
+    const cuuint32_t box[3] = {64, kD, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, p->pool_codes, dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return GDN_ERR_CUDA;

@@ -134,11 +134,17 @@ struct PrefillArgs {
   uint8_t* pool_codes;
   uint8_t* pool_scales;
   float* pool_gs;
+  int64_t code_stride, scale_stride, gs_stride;  // bytes between consecutive (slot, head) tiles
   __nv_bfloat16* out;
   float q_scale, gden;
   float* debug_y;
   uint32_t* status;
 };
+
+// The global scale of pool tile pt (slot * HV + head).
+__device__ __forceinline__ float* gs_at(const PrefillArgs& a, int64_t pt) {
+  return reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.pool_gs) + pt * a.gs_stride);
+}
 
 // Byte offsets in the no-swizzle K-major layouts (16-byte K chunks 128 bytes
 // apart, 8-row groups sbo apart).
@@ -601,13 +607,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* const sf_one = sf + kScaleBytes;
           {
             const int r = ctid >> 1, c0 = 2 * (ctid & 1);
-            const uint4* src = reinterpret_cast<const uint4*>(a.pool_codes + pt * kCodeBytes + r * 64 + 16 * c0);
+            const uint4* src = reinterpret_cast<const uint4*>(a.pool_codes + pt * a.code_stride + r * 64 + 16 * c0);
             const uint4 x0 = __ldg(src), x1 = __ldg(src + 1);
             *reinterpret_cast<uint4*>(codes + 2048 * c0 + 16 * r) = x0;
             *reinterpret_cast<uint4*>(codes + 2048 * (c0 + 1) + 16 * r) = x1;
             const int t = ctid >> 7, m0 = (ctid & 127) >> 2, m1 = ctid & 3;
             reinterpret_cast<uint32_t*>(sf)[t * 128 + m0 * 4 + m1] =
-                __ldg(reinterpret_cast<const uint32_t*>(a.pool_scales + pt * kScaleBytes) + (32 * m1 + m0) * 2 + t);
+                __ldg(reinterpret_cast<const uint32_t*>(a.pool_scales + pt * a.scale_stride) + (32 * m1 + m0) * 2 + t);
             reinterpret_cast<uint32_t*>(sf_one)[ctid] = 0x38383838u;  // UE4M3 1.0
             for (int e = ctid; e < (int)kCodeBytes; e += kGroup) {
               const int rr = e >> 6, byte = e & 63;
@@ -617,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ident[canon(rr, byte)] = val;
             }
           }
-          const float gs = __ldg(a.pool_gs + pt);
+          const float gs = __ldg(gs_at(a, pt));
           tc::fence_smem_to_async();
           tc::fence_before_sync();
           group_sync(kBarChain);
@@ -821,11 +827,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           requant_half_row<kMode>(
               x, am, __frcp_rn(gs_new), ms.inv_tab, words, scw,
               a.debug_y ? a.debug_y + (((int64_t)cur.n * a.HV + h) * kD + i) * kD + 64 * hh : nullptr);
-          uint4* dst = reinterpret_cast<uint4*>(a.pool_codes + pt * kCodeBytes + i * 64 + 32 * hh);
+          uint4* dst = reinterpret_cast<uint4*>(a.pool_codes + pt * a.code_stride + i * 64 + 32 * hh);
           dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
           dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
-          *reinterpret_cast<uint32_t*>(a.pool_scales + pt * kScaleBytes + i * 8 + 4 * hh) = scw;
-          if (ctid == 0) a.pool_gs[pt] = gs_new;
+          *reinterpret_cast<uint32_t*>(a.pool_scales + pt * a.scale_stride + i * 8 + 4 * hh) = scw;
+          if (ctid == 0) *gs_at(a, pt) = gs_new;
         }
         group_sync(kBarChain);  // the transpose buffer is read
         if (ctid == 0) mbar_arrive(&ms.bar_seq);  // the prep group's scratch is free again
@@ -892,6 +898,10 @@ extern "C" int gdn_prefill(const gdn_prefill_params* p, cudaStream_t stream) {
   if (p->num_seqs == 0 || p->total_tokens == 0) return GDN_OK;
   if (!p->q || !p->k || !p->v || !p->g || !p->beta || !p->cu_seqlens || !p->out) return GDN_ERR_ARGS;
   if (p->slot_idx && (!p->pool_codes || !p->pool_scales || !p->pool_gscale)) return GDN_ERR_ARGS;
+  int64_t code_stride = 0, scale_stride = 0, gs_stride = 0;
+  if (p->slot_idx && !pool_strides(p->pool_tile_stride, p->pool_codes, p->pool_scales, p->pool_gscale,
+                                   &code_stride, &scale_stride, &gs_stride))
+    return GDN_ERR_ALIGN;
   if (p->total_tokens > INT32_MAX) return GDN_ERR_UNSUPPORTED;  // cu_seqlens are int32
   const int64_t nitems = (int64_t)p->num_seqs * p->num_v_heads;
   if (nitems > INT32_MAX / 2) return GDN_ERR_UNSUPPORTED;
@@ -921,6 +931,9 @@ extern "C" int gdn_prefill(const gdn_prefill_params* p, cudaStream_t stream) {
   a.pool_codes = p->pool_codes;
   a.pool_scales = p->pool_scales;
   a.pool_gs = p->pool_gscale;
+  a.code_stride = code_stride;
+  a.scale_stride = scale_stride;
+  a.gs_stride = gs_stride;
   a.out = p->out;
   a.q_scale = p->q_scale > 0.0f ? p->q_scale : 0.08838834764831845f;  // 1/sqrt(128)
   a.gden = p->gscale_den > 0.0f ? p->gscale_den : default_gden(p->scale_mode);

@@ -108,6 +108,66 @@ __device__ __forceinline__ void requant_blocks(const float2 (&x)[8 * NB], const 
   }
 }
 
+// ---- power-of-two global scale ---------------------------------------------
+//
+// The decode requantiser picks the new global scale as gs' = c * 2^-k, where
+// S' = c * D (D the fp32 tile it holds) and k >= 0 is the largest integer with
+// max |D| * 2^k <= gden, and quantises y = D * 2^k.  Scaling by 2^k is exact,
+// so everything the reference quantiser derives from y follows from D:
+//   * a block's max |y| is am * 2^k and its local scale RN(am * 2^k / 6) is
+//     2^k RN(am / 6) (am / 6 a normal float);
+//   * the scale byte, while it lies in [8, saturation] (a normal E4M3 code
+//     with no clamping), is the code of RN(am / 6) plus 8k: scale_w() - 960 + 8k;
+//   * the inverse of that scale is RN(1 / dec) = scale_inv_w() * 2^-k, so
+//     RN(y * inv) = RN(D * scale_inv_w()), which does not depend on k.
+// The E2M1 codes of a block can therefore be computed before the tile max is
+// known, with one multiply per element fewer than y = D * 2^k, v = y * inv.
+// Blocks whose final scale byte falls outside [8, saturation] (a subnormal
+// or zero local scale, saturation) or that hold a NaN take the exact path.
+
+// The scale encoder's rounding of x = RN(am / 6) for a finite am > 0 with x a
+// normal float, as (biased exponent << 3 | 3 mantissa bits): half up at the
+// third mantissa bit, a significand >= 1.875 to the next binade
+// (src/intrinsics/gdn_fp4_intrinsics.cuh:102-120).  For x >= 2^-6 the E4M3
+// code is this value - 960; the decoded scale is the float with bits w << 20.
+__device__ __forceinline__ uint32_t scale_w(float am) {
+  const uint32_t u = __float_as_uint(div6_for_scale(am));
+  const uint32_t add = ((u & 0x700000u) == 0x700000u) ? 0x100000u : 0x80000u;
+  return (u + add) >> 20;
+}
+
+// rt[m] = bits of RN(1 / (1 + m/8)) + (127 << 23) for m = 0..7 (scale_inv_w_entry).
+// RN(1 / dec) of the decoded scale with bits w << 20 is then
+// rt[w & 7] - ((w >> 3) << 23): the reciprocal's significand from the table
+// and its exponent 127 - (biased exponent of dec), exact while both are
+// normal floats.
+__device__ __forceinline__ float scale_inv_w(uint32_t w, const uint32_t* rt) {
+  return __uint_as_float(rt[w & 7u] - ((w & ~7u) << 20));
+}
+
+// RN(1 / (1 + m / 8)) for m = 0..7, correctly rounded (the reciprocals of
+// 8/8 .. 15/8), as float bit patterns plus 127 << 23.
+__host__ __device__ constexpr uint32_t scale_inv_w_entry(int m) {
+  return (m == 0 ? 0x3F800000u    // 1
+          : m == 1 ? 0x3F638E39u  // 8/9
+          : m == 2 ? 0x3F4CCCCDu  // 8/10
+          : m == 3 ? 0x3F3A2E8Cu  // 8/11
+          : m == 4 ? 0x3F2AAAABu  // 8/12
+          : m == 5 ? 0x3F1D89D9u  // 8/13
+          : m == 6 ? 0x3F124925u  // 8/14
+                   : 0x3F088889u) // 8/15
+         + (127u << 23);
+}
+
+// k = the largest integer with A * 2^k <= gden, for normal positive floats A
+// and gden, from their bit patterns.
+__device__ __forceinline__ int pow2_headroom(uint32_t a_bits, uint32_t gden_bits) {
+  return (int)(gden_bits >> 23) - (int)(a_bits >> 23) - ((a_bits & 0x7FFFFFu) > (gden_bits & 0x7FFFFFu) ? 1 : 0);
+}
+
+// 2^e for an integer e in [-126, 127].
+__device__ __forceinline__ float exp2i(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
+
 // The 64-element form used by the prefill epilogue.
 template <int kMode>
 __device__ __forceinline__ void requant_half_row(const float2 (&x)[32], const float (&am)[4], float inv_gs,

@@ -68,6 +68,7 @@ class DecodeParams(ctypes.Structure):
         ("A_log", _p), ("dt_bias", _p), ("gate_a", _p), ("gate_b", _p), ("gate_stride", _i64),
         ("qk_l2norm", _i32),
         ("norm_weight", _p), ("gate_z", _p), ("z_stride", _i64), ("norm_eps", _f32), ("norm_act", _i32),
+        ("pool_tile_stride", _i64),
     ]
 
 
@@ -84,6 +85,7 @@ class PrefillParams(ctypes.Structure):
         ("out", _p),
         ("q_scale", _f32), ("scale_mode", _i32), ("gscale_den", _f32),
         ("debug_y", _p),
+        ("pool_tile_stride", _i64),
     ]
 
 

@@ -218,6 +218,7 @@ def decode(q, k, v, g, beta, slot_idx, pool, out=None, q_scale: float = 0.0, deb
     p.q_stride, p.k_stride, p.v_stride = q.stride(0), k.stride(0), v.stride(0)
     p.g, p.beta, p.slot_idx = _ptr(g), _ptr(beta), slot_idx.data_ptr()
     p.pool_codes, p.pool_scales, p.pool_gscale = pool.codes.data_ptr(), pool.scales.data_ptr(), pool.gscale.data_ptr()
+    p.pool_tile_stride = pool.tile_stride
     p.out = out.data_ptr()
     p.q_scale = q_scale
     p.scale_mode = pool.scale_mode
@@ -283,6 +284,7 @@ def prefill(q, k, v, g, beta, cu_seqlens, pool=None, slot_idx=None, has_initial_
         p.slot_idx = slot_idx.data_ptr()
         p.pool_codes, p.pool_scales = pool.codes.data_ptr(), pool.scales.data_ptr()
         p.pool_gscale = pool.gscale.data_ptr()
+        p.pool_tile_stride = pool.tile_stride
         p.scale_mode, p.gscale_den = pool.scale_mode, pool.gscale_den
     p.out = out.data_ptr()
     p.q_scale = q_scale
@@ -294,6 +296,8 @@ def prefill(q, k, v, g, beta, cu_seqlens, pool=None, slot_idx=None, has_initial_
 # ---- pool ----------------------------------------------------------------------------
 
 def pool_gather(pool, slot_idx: torch.Tensor):
+    if pool.tile_stride:
+        raise ValueError("gdn_pool_gather copies dense pools; index a record pool's views instead")
     n = slot_idx.numel()
     HV, D = pool.num_v_heads, pool.head_dim
     codes = torch.empty((n, HV, D, D // 2), dtype=torch.uint8, device=pool.codes.device)
@@ -307,6 +311,8 @@ def pool_gather(pool, slot_idx: torch.Tensor):
 
 
 def pool_scatter(pool, slot_idx: torch.Tensor, codes, scales, gs) -> None:
+    if pool.tile_stride:
+        raise ValueError("gdn_pool_scatter copies dense pools; index a record pool's views instead")
     n = slot_idx.numel()
     check("gdn_pool_scatter",
           lib.gdn_pool_scatter(codes.data_ptr(), scales.data_ptr(), gs.data_ptr(), pool.num_slots, pool.num_v_heads,

@@ -10,11 +10,14 @@ with a per-token Python loop (qwen35_gdn_patch.py:66-124, 166-200); vLLM 0.22
 runs these layers in ``vllm.model_executor.layers.mamba.gdn.qwen_gdn_linear_attn``,
 so ``apply`` installs the seam there instead:
 
+* the layer's ``get_state_shape`` / ``get_state_dtype`` make vLLM allocate
+  its recurrent state cache as NVFP4 records (uint8 [blocks, HV, 9232],
+  gdn_b200.vllm_seam.state_shape), so the state stays NVFP4 in the cache;
 * the ``chunk_gated_delta_rule`` CustomOp (prefill) calls
   gdn_b200.vllm_seam.chunk_gated_delta_rule (the chunked NVFP4 prefill);
-* the module's ``fused_sigmoid_gating_delta_rule_update`` (decode) calls
-  gdn_b200.vllm_seam.fused_sigmoid_gating_delta_rule_update (the fused NVFP4
-  decode).
+* the module's ``fused_sigmoid_gating_delta_rule_update`` and
+  ``fused_recurrent_gated_delta_rule_packed_decode`` (decode) call the fused
+  NVFP4 decode, which updates the records in place.
 
 Usage::
 
@@ -86,12 +89,16 @@ def _resolve_so(so_path: str | None) -> str:
     return so_path
 
 
-def apply(so_path: str | None = None) -> None:
+def apply(so_path: str | None = None, nvfp4_cache: bool = True) -> None:
     """Load the GDN op library and route vLLM's gated delta net layer through it.
 
     Args:
         so_path: path to libgdn_sm120_op.so.  Falls back to $GDN_OP_LIB, then the
                  in-tree build.
+        nvfp4_cache: keep the recurrent state in vLLM's cache as NVFP4 records
+                 (layers built after apply(); the cache is sized from the
+                 patched get_state_shape / get_state_dtype).  False keeps
+                 vLLM's dense cache, crossing into NVFP4 at every call.
     """
     global _patched, _so_path
     with _lock:
@@ -120,9 +127,26 @@ def apply(so_path: str | None = None) -> None:
             if hasattr(cls, name):
                 _originals[(cls, name)] = cls.__dict__.get(name, _INHERITED)
                 setattr(cls, name, _prefill)
-        _originals[(mod, "fused_sigmoid_gating_delta_rule_update")] = mod.__dict__.get(
-            "fused_sigmoid_gating_delta_rule_update", _INHERITED)
-        mod.fused_sigmoid_gating_delta_rule_update = vllm_seam.fused_sigmoid_gating_delta_rule_update
+        for name in ("fused_sigmoid_gating_delta_rule_update", "fused_recurrent_gated_delta_rule_packed_decode"):
+            if hasattr(mod, name):
+                _originals[(mod, name)] = mod.__dict__.get(name, _INHERITED)
+                setattr(mod, name, getattr(vllm_seam, name))
+        if nvfp4_cache:
+            layer = mod.QwenGatedDeltaNetAttention
+            orig_shape = layer.get_state_shape
+            orig_dtype = layer.get_state_dtype
+
+            def get_state_shape(self):
+                conv_shape, temporal = orig_shape(self)
+                return conv_shape, vllm_seam.state_shape(temporal[0])
+
+            def get_state_dtype(self):
+                conv_dtype = orig_dtype(self)[0]
+                return conv_dtype, vllm_seam.state_dtype()
+
+            for name, fn in (("get_state_shape", get_state_shape), ("get_state_dtype", get_state_dtype)):
+                _originals[(layer, name)] = layer.__dict__.get(name, _INHERITED)
+                setattr(layer, name, fn)
         _so_path = so_path
         _patched = True
         print(f"[gdn_patch] Applied GDN router patch -- so={so_path}")

@@ -191,6 +191,15 @@ typedef struct gdn_decode_params {
   int64_t z_stride;         /* elements between sequences (a multiple of 8); 0 = HV * D */
   float norm_eps;           /* > 0 */
   int32_t norm_act;         /* 0: SiLU, 1: sigmoid */
+  /* Pool layout.  0: the three dense arrays above.  Otherwise the record
+   * layout, in which every (slot, head) tile is one record of this many bytes
+   * (a multiple of 16, at least 9220) holding its codes at byte 0, its scales
+   * at byte 8192 and its global scale at byte 9216: pool_codes, pool_scales
+   * and pool_gscale then point at bytes 0, 8192 and 9216 of the first record,
+   * and all three advance by the record size.  A serving engine that
+   * allocates one byte array per layer for its recurrent state (vLLM's
+   * mamba state cache) holds the pool in it this way. */
+  int64_t pool_tile_stride;
 } gdn_decode_params;
 
 GDN_API int gdn_decode(const gdn_decode_params* params, cudaStream_t stream);
@@ -231,6 +240,7 @@ typedef struct gdn_prefill_params {
   int32_t scale_mode;     /* GDN_SCALE_* */
   float gscale_den;       /* <= 0 selects 6*saturation */
   float* debug_y;         /* optional [N, HV, D, D]: fp32 quantiser inputs of the final states */
+  int64_t pool_tile_stride; /* pool layout, as in gdn_decode_params (0: dense arrays) */
 } gdn_prefill_params;
 
 GDN_API int gdn_prefill(const gdn_prefill_params* params, cudaStream_t stream);

@@ -228,6 +228,43 @@ ORC_API void orc_legacy_op(const uint8_t* S_data, const uint8_t* S_scales, const
  * quantised by the reference quantiser.  A negative slot marks padding: the
  * pool is not touched and o is zero.  Optional y_out receives the fp32
  * quantiser inputs per tile ([B][HV][D*D]). */
+/* ---- decode-step requantisation (new; the decode kernel's rule) -------------
+ * S' = c * D with c = 2^7 * RN(expf(g) * gs) (c = 1 when RN(expf(g) * gs) is
+ * below 1e-30, where the decode kernel drops the decayed state) and
+ * D = RN(S' / c).  With A = max |D| (NaN ignored):
+ *   A finite > 0: k = the largest integer with A * 2^k <= gden, clamped to
+ *                 [-126, 126]; gs' = c * 2^-k and y = D * 2^k;
+ *   A = 0:        gs' = 1 and y = D * c;
+ *   A = inf:      gs' = inf and y = D * 0;
+ * then the reference quantiser on y. */
+static void requant_pow2(const float* Sn, int64_t n, float c, uint8_t* codes, uint8_t* scales, float* gs_out,
+                         float* y_out, int mode, float gden) {
+  float* y = y_out ? y_out : (float*)malloc((size_t)n * sizeof(float));
+  float A = 0.0f;
+  for (int64_t i = 0; i < n; ++i) {
+    y[i] = (float)((double)Sn[i] / (double)c);
+    A = fmaxf(A, fabsf(y[i]));
+  }
+  float mult, gs;
+  if (A > 0.0f && isfinite(A)) {
+    int k = 0;
+    while (ldexpf(A, k + 1) <= gden && k < 126) ++k;
+    while (ldexpf(A, k) > gden && k > -126) --k;
+    mult = ldexpf(1.0f, k);
+    gs = c * ldexpf(1.0f, -k);
+  } else if (A == 0.0f) {
+    mult = c;
+    gs = 1.0f;
+  } else {
+    mult = 0.0f;
+    gs = INFINITY;
+  }
+  for (int64_t i = 0; i < n; ++i) y[i] = y[i] * mult;
+  orc_quantise(y, codes, scales, n, mode);
+  *gs_out = gs;
+  if (!y_out) free(y);
+}
+
 ORC_API void orc_gdn_decode(int B, int HK, int HV, int D,
                             const uint16_t* q, const uint16_t* k, const uint16_t* v,
                             const float* g, const float* beta, const int32_t* slot,
@@ -259,8 +296,12 @@ ORC_API void orc_gdn_decode(int B, int HK, int HV, int D,
       const int64_t t = (int64_t)s * HV + h;
       uint8_t* pc = pool_codes + t * (DD / 2);
       uint8_t* ps = pool_scales + t * (DD / 16);
-      orc_dequantise_tile_gs(pc, ps, pool_gs[t], S, DD, mode);
-      const double alpha = exp((double)g[(int64_t)b * HV + h]);
+      const float pool_gs_in = pool_gs[t];
+      orc_dequantise_tile_gs(pc, ps, pool_gs_in, S, DD, mode);
+      /* the decode kernel drops the decayed state when alpha * gs < 1e-30 in fp32 */
+      const float cg = expf(g[(int64_t)b * HV + h]) * pool_gs_in;
+      const int drop = cg >= 0.0f && cg < 1e-30f;
+      const double alpha = drop ? 0.0 : exp((double)g[(int64_t)b * HV + h]);
       const double bt = beta[(int64_t)b * HV + h];
       for (int j = 0; j < D; ++j) u[j] = 0.0;
       for (int i = 0; i < D; ++i) {
@@ -286,8 +327,8 @@ ORC_API void orc_gdn_decode(int B, int HK, int HV, int D,
           o_bf16[ob + j] = (uint16_t)(isnan(of) ? 0x7FC0u : (r >> 16));
         }
       }
-      orc_quantise_tile_gs(Sn, DD, pc, ps, &pool_gs[t],
-                           y_out ? y_out + ((int64_t)b * HV + h) * DD : NULL, mode, gden);
+      const float c = drop ? 1.0f : cg * 128.0f;
+      requant_pow2(Sn, DD, c, pc, ps, &pool_gs[t], y_out ? y_out + ((int64_t)b * HV + h) * DD : NULL, mode, gden);
     }
   }
   free(S); free(Sn); free(u); free(w); free(oo);

@@ -106,3 +106,27 @@ def test_ctypes_mirrors_match_the_c_layout(tmp_path, struct_name, py_name):
     out = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
     assert out[0] == ctypes.sizeof(py)
     assert out[1:] == [getattr(py, f).offset for f in fields]
+
+
+def test_python_param_structs_match_the_header(tmp_path):
+    """The ctypes mirrors of gdn_decode_params / gdn_prefill_params have the C
+    layout: same size and the same offset of every field."""
+    import subprocess
+    from gdn_b200 import _capi
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "gdn_b200.h"', 'int main(void) {']
+    for cname, py in (("gdn_decode_params", _capi.DecodeParams), ("gdn_prefill_params", _capi.PrefillParams)):
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for name, _ in py._fields_:
+            lines.append(f'  printf("{cname} {name} %zu\\n", offsetof({cname}, {name}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", f"-I{ROOT / 'include'}", "-I/usr/local/cuda/include", str(src), "-o", str(exe)],
+                   check=True)
+    got = dict(line.rsplit(" ", 1) for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                                check=True).stdout.splitlines())
+    for cname, py in (("gdn_decode_params", _capi.DecodeParams), ("gdn_prefill_params", _capi.PrefillParams)):
+        assert int(got[f"{cname} size"]) == ctypes.sizeof(py), cname
+        for name, _ in py._fields_:
+            assert int(got[f"{cname} {name}"]) == getattr(py, name).offset, (cname, name)

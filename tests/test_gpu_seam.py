@@ -141,3 +141,104 @@ def test_seam_decode_out_of_place(cuda):
             assert not torch.equal(final[i], ssm[s])
         else:
             assert int(final[i].count_nonzero()) == 0
+
+
+def _sqnr(ref: np.ndarray, test: np.ndarray) -> float:
+    ref = ref.astype(np.float64)
+    err = test.astype(np.float64) - ref
+    return float(10 * np.log10((ref ** 2).sum() / max((err ** 2).sum(), 1e-300)))
+
+
+def test_nvfp4_state_cache_prefill_then_8_decodes_matches_vllm(cuda, oracle_lib):
+    """vLLM's own call sequence for a GDN layer (qwen_gdn_linear_attn.py
+    _forward_core / _forward_core_decode_non_spec): a varlen prefill through
+    the ChunkGatedDeltaRule op with the sequences' gathered states, the
+    index_put of the final states into the cache, then 8 packed decode steps
+    updating the cache in place at the state indices.  Patched: the cache is
+    uint8 NVFP4 records and the seam runs the NVFP4 kernels.  Unpatched: vLLM's
+    own FLA kernels on a dense fp32 cache.  The gate: the seam's outputs,
+    measured against vLLM's, are within 0.1 dB of the oracle's quantised
+    recurrence (same inputs, same NVFP4 state) measured the same way."""
+    fla = pytest.importorskip("vllm.model_executor.layers.fla.ops")
+    from gdn_b200 import vllm_seam, workloads
+    from gdn_b200.pool import RECORD_BYTES, NVFP4StatePool
+    lengths = [70, 130, 33, 200]
+    N, steps, blocks = len(lengths), 8, 9
+    block_idx = torch.tensor([3, 7, 1, 5], dtype=torch.int32, device="cuda")  # 0 is vLLM's null block
+    x = workloads.token_inputs(sum(lengths), HK, HV, D, seed=70, device="cuda")  # q, k L2-normalised
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int32, device="cuda")
+    gen = torch.Generator().manual_seed(71)
+    A_log = (torch.rand(HV, generator=gen) * 2 - 1).cuda()
+    dt_bias = torch.randn(HV, generator=gen).cuda()
+    dec = workloads.decode_steps(N, steps, HK, HV, D, seed=72, device="cuda")
+    a = torch.randn((steps, N, HV), generator=gen).to(torch.bfloat16).cuda()
+    b = torch.randn((steps, N, HV), generator=gen).to(torch.bfloat16).cuda()
+    qkv_raw = []  # decode inputs as vLLM's packed rows, q / k not normalised (the kernels normalise)
+    for t in range(steps):
+        scale = 0.5 + torch.rand((N, 1, 1), generator=gen).cuda()
+        qkv_raw.append(torch.cat([(dec["q"][t] * scale).reshape(N, -1), (dec["k"][t] * scale).reshape(N, -1),
+                                  dec["v"][t].reshape(N, -1)], dim=1).to(torch.bfloat16).contiguous())
+    q1, k1, v1 = x["q"].unsqueeze(0), x["k"].unsqueeze(0), x["v"].unsqueeze(0)
+    g1, b1 = x["g"].unsqueeze(0), x["beta"].unsqueeze(0)
+
+    def run(cache, prefill_fn, decode_fn):
+        idx = block_idx.long()
+        init = cache[idx].contiguous()
+        init[...] = 0  # no sequence has an initial state (vLLM zeroes those rows)
+        o_pre, final = prefill_fn(q1, k1, v1, g1, b1, init)
+        cache[idx] = final.to(cache.dtype)
+        outs = [o_pre[0].float().cpu().numpy()]
+        for t in range(steps):
+            out = torch.empty((N, 1, HV, D), dtype=torch.bfloat16, device="cuda")
+            decode_fn(qkv_raw[t], a[t], b[t], cache, out)
+            outs.append(out[:, 0].float().cpu().numpy())
+        torch.cuda.synchronize()
+        return outs
+
+    dense = torch.zeros((blocks, HV, D, D), dtype=torch.float32, device="cuda")
+    ref = run(dense,
+              lambda q, k, v, g, be, init: fla.chunk_gated_delta_rule(
+                  q=q, k=k, v=v, g=g, beta=be, initial_state=init, output_final_state=True, cu_seqlens=cu,
+                  use_qk_l2norm_in_kernel=False),
+              lambda qkv, aa, bb, cache, out: fla.fused_recurrent_gated_delta_rule_packed_decode(
+                  mixed_qkv=qkv, a=aa, b=bb, A_log=A_log, dt_bias=dt_bias, scale=D ** -0.5, initial_state=cache,
+                  out=out, ssm_state_indices=block_idx, use_qk_l2norm_in_kernel=True))
+    records = torch.zeros((blocks, HV, RECORD_BYTES), dtype=torch.uint8, device="cuda")
+    got = run(records,
+              lambda q, k, v, g, be, init: vllm_seam.chunk_gated_delta_rule(
+                  q, k, v, g, be, init, True, cu_seqlens=cu, use_qk_l2norm_in_kernel=False),
+              lambda qkv, aa, bb, cache, out: vllm_seam.fused_recurrent_gated_delta_rule_packed_decode(
+                  qkv, aa, bb, A_log, dt_bias, D ** -0.5, cache, out, block_idx, use_qk_l2norm_in_kernel=True))
+    assert records.dtype == torch.uint8 and records.shape == (blocks, HV, RECORD_BYTES)
+    assert int(records[0].count_nonzero()) == 0  # the null block is never written
+
+    # the oracle: f64 prefill from zero, its final state through the reference
+    # quantiser (the prefill's global scale amax / (6 * 448)), then 8 oracle decode steps
+    qf, kf, vf = (x[n].float().cpu().numpy() for n in ("q", "k", "v"))
+    gf, bfv = x["g"].cpu().numpy(), x["beta"].cpu().numpy()
+    cun = cu.cpu().numpy()
+    S_end = np.zeros((N, HV, D, D))
+    for n in range(N):
+        s0, s1 = cun[n], cun[n + 1]
+        for h in range(HV):
+            _, S_end[n, h] = oracle_lib.recurrent_f64(np.zeros((D, D)), qf[s0:s1, h // 2], kf[s0:s1, h // 2],
+                                                      vf[s0:s1, h], gf[s0:s1, h], bfv[s0:s1, h], QS)
+    c0, s0_, g0, _ = oracle_lib.quantise_tiles(S_end.astype(np.float32).reshape(-1), D * D, 1)
+    codes = c0.reshape(N, HV, D, D // 2).copy()
+    scales = s0_.reshape(N, HV, D, D // 16).copy()
+    gsc = g0.reshape(N, HV).copy()
+    orc = [None]
+    for t in range(steps):
+        qkv = qkv_raw[t].view(N, 2 * HK + HV, D)
+        qn = vllm_seam.l2norm(qkv[:, :HK])
+        kn = vllm_seam.l2norm(qkv[:, HK:2 * HK])
+        gt, bt = vllm_seam.gating(A_log, a[t], b[t], dt_bias)
+        o32, _, _ = oracle_lib.gdn_decode(_bits(qn), _bits(kn), _bits(qkv[:, 2 * HK:]), gt.cpu().numpy(),
+                                          bt.cpu().numpy(), np.arange(N, dtype=np.int32), codes, scales, gsc, QS, 1)
+        orc.append(o32)
+    pre = _sqnr(ref[0], got[0])
+    assert pre >= 40.0, pre  # the prefill from a zero state: fp32 arithmetic only
+    for t in range(1, steps + 1):
+        s_gpu, s_orc = _sqnr(ref[t], got[t]), _sqnr(ref[t], orc[t])
+        print(f"decode step {t}: SQNR vs vLLM, seam {s_gpu:.2f} dB, oracle {s_orc:.2f} dB")
+        assert s_gpu >= s_orc - 0.1, (t, s_gpu, s_orc)
