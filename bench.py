@@ -64,7 +64,8 @@ def _config(n_gpus: int) -> dict:
     return {"workload": WORKLOAD, "batch_per_gpu": B, "num_k_heads": HK, "num_v_heads": HV, "head_dim": D,
             "pool_slots": NUM_SLOTS, "state_format": "nvfp4 e2m1 + ue4m3/16 + fp32 per-head global scale",
             "scale_mode": "fn448, gs = amax/(6*448)", "parallelism": f"dp{n_gpus} (sequences sharded, no collective)",
-            "l2": f"inputs rotate over {N_POOLS} pools + input sets (453 MB > 126 MB L2)"}
+            "l2": f"inputs rotate over {N_POOLS} pools + input sets (453 MB > 126 MB L2)",
+            "launch": "K steps replayed from one CUDA graph (eager with --eager)"}
 
 
 # ---- clocks -----------------------------------------------------------------------------
@@ -251,6 +252,21 @@ def cpu_decode_sample(seconds: float, threads: int | None = None) -> dict:
 
 # ---- GPU path ---------------------------------------------------------------------------------------
 
+def _capture(args, dev, stream, step):
+    """The K timed steps (warm-up offsets continue) captured in one CUDA graph."""
+    import torch
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g, stream=side):
+            for i in range(args.steps):
+                step(args.warmup + i)
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    return g
+
+
 def run_ours(args, dist, rank, world, local) -> dict | None:
     import torch
     from gdn_b200 import NVFP4StatePool, ops, workloads
@@ -287,17 +303,26 @@ def run_ours(args, dist, rank, world, local) -> dict | None:
     # set-up overlaps the previous one's tail (programmatic dependent launch),
     # so the mean launch duration is the timed region over K.  Event pairs
     # around every launch would serialise the launches and add their own cost.
+    # The K steps are replayed from a CUDA graph, as a serving engine launches
+    # its decode step (the graph keeps the programmatic dependencies), so no
+    # host launch latency sits between or before them; --eager launches them
+    # one by one from Python instead.
+    graph = _capture(args, dev, stream, step) if not args.eager else None
     t_begin = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     _barrier(dist)
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
         t_begin.record(stream)
-        for i in range(args.steps):
-            step(args.warmup + i)
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(args.steps):
+                step(args.warmup + i)
         t_end.record(stream)
         torch.cuda.synchronize()
     _barrier(dist)
+    del graph
     own_ms = t_begin.elapsed_time(t_end)
     total_ms = _max_over_ranks(dist, own_ms)
     spread = _rank_spread(dist, own_ms / args.steps)
@@ -437,9 +462,10 @@ def _peaks() -> dict:
     return json.loads(p.read_text()) if p.exists() else {}
 
 
-def _timed(args, dist, stream, step, local):
+def _timed(args, dist, stream, step, local, graph_ok: bool = False):
     """W warm-up steps, then K steps between barriers; returns (max-over-ranks
-    total ms, per-step event pairs, clock summary)."""
+    total ms, clock summary).  With graph_ok (and without --eager) the K steps
+    are replayed from one CUDA graph."""
     import torch
     from gdn_b200 import ops
     for i in range(args.warmup):
@@ -447,17 +473,22 @@ def _timed(args, dist, stream, step, local):
     torch.cuda.synchronize()
     if ops.device_status(clear=True):
         raise RuntimeError("device status set during warm-up")
+    graph = _capture(args, stream.device, stream, step) if graph_ok and not args.eager else None
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     _barrier(dist)
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
         t0.record(stream)
-        for i in range(args.steps):
-            step(args.warmup + i)
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(args.steps):
+                step(args.warmup + i)
         t1.record(stream)
         torch.cuda.synchronize()
     _barrier(dist)
+    del graph
     if ops.device_status(clear=True):
         raise RuntimeError("device status set during the timed region")
     own = t0.elapsed_time(t1)
@@ -642,8 +673,9 @@ def run_layers(args, dist, rank, world, local) -> dict | None:
             x = inputs[layer]
             ops.decode(x["q"], x["k"], x["v"], x["g"], x["beta"], slots[layer], pools[layer], out=out)
 
-    total_ms, clocks = _timed(args, dist, stream, step, local)
-    launch_ms = _max_over_ranks(dist, _kernel_ms(args, stream, step) / LAYERS)
+    total_ms, clocks = _timed(args, dist, stream, step, local, graph_ok=True)
+    # one decode launch per layer, back to back: the mean launch is the step over the layers
+    launch_ms = total_ms / args.steps / LAYERS
     if rank != 0:
         return None
     peaks = _peaks()
@@ -696,6 +728,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="launch the timed steps one by one from Python instead of replaying a CUDA graph")
     ap.add_argument("--workload", choices=["decode", "prefill", "mixed", "layers"], default="decode",
                     help="decode: batch-256 decode step (the headline); prefill: 8 x 8192-token chunked "
                          "prefill; mixed: 48 varlen prefills + 512 decodes; layers: 36-layer TP decode stack")

@@ -439,29 +439,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     // ===================================== MMA =====================================
+    // Every shared-memory descriptor, TMEM address and mbarrier address is
+    // formed once here: a stage's descriptors are the first stage's plus the
+    // stage offset (the start-address field holds address >> 4), so issuing a
+    // tcgen05 operation costs a few instructions instead of a chain of 64-bit
+    // address arithmetic on the critical path.
     const uint32_t id_mx = tc::idesc_mxf4nvf4(128, 128);
     const uint32_t id_r1 = tc::idesc_tf32(128, 128);
+    constexpr uint32_t kStageDesc = sizeof(Stage) >> 4;
+    const uint64_t d_ident0 = tc::smem_desc(sm.ident, 2048, 128);
+    const uint64_t d_ident1 = tc::smem_desc(sm.ident + 4096, 2048, 128);
+    const uint64_t d_codes = desc_codes(sm.st[0].codes, 0);  // + 2: the second K step (32 bytes)
+    const uint64_t d_sfp = tc::smem_desc(sm.st[0].sfp, 0, 128);  // + 32: the second K step (512 bytes)
+    const uint64_t d_ak = tc::smem_desc(sm.st[0].ak, 128, 256);
+    const uint64_t d_bw0 = tc::smem_desc(sm.bw[0], 128, 256);
+    const uint64_t d_bw1 = tc::smem_desc(sm.bw[1], 128, 256);
+    const uint32_t t_one = T + kColOne, t_d1t = T + kColD1t;
+    const uint32_t b_t = smem_u32(&sm.bar_t), b_d0 = smem_u32(&sm.bar_d[0]), b_empty0 = smem_u32(&sm.empty[0]);
     if (lane == 0)
-      for (int kt = 0; kt < 2; ++kt) tc::cp_32x128b_warpx4(T + kColOne + 4 * kt, tc::smem_desc(sm.sf_one + 512 * kt, 0, 128));
+      for (int kt = 0; kt < 2; ++kt) tc::cp_32x128b_warpx4(t_one + 4 * kt, tc::smem_desc(sm.sf_one + 512 * kt, 0, 128));
     bool ok = true;
     // Tile n: scale factors to TMEM and MMA1' into D1' (free: the w warps
     // loaded tile n - 1's).
     auto front = [&](int n, bool& more) -> bool {
-      const int s = n % kStages;
+      const uint32_t s = (uint32_t)n & (kStages - 1);
       if (!wait_bar(&sm.ready[s], (uint32_t)((n / kStages) & 1), abort_flag)) return false;
-      more = !sm.ring[n % kRing].end;
+      more = !sm.ring[n & (kRing - 1)].end;
       if (!more) return true;
       if (n >= 1 && !wait_bar(&sm.bar_tfree, (uint32_t)((n - 1) & 1), abort_flag)) return false;
       tc::fence_after_sync();
       if (lane == 0) {
-        Stage& st = sm.st[s];
-        const uint32_t sf = T + kColSF + 8 * (n % 3);
-        for (int kt = 0; kt < 2; ++kt) tc::cp_32x128b_warpx4(sf + 4 * kt, tc::smem_desc(st.sfp + 512 * kt, 0, 128));
-        for (int kt = 0; kt < 2; ++kt)
-          tc::mma_mxf4nvf4(T + kColD1t, tc::smem_desc(sm.ident + 4096 * kt, 2048, 128), desc_codes(st.codes, kt),
-                           id_mx, T + kColOne + 4 * kt, sf + 4 * kt, kt > 0);
+        const uint64_t so = s * kStageDesc;
+        const uint32_t sf = T + kColSF + 8 * (uint32_t)(n % 3);
+        tc::cp_32x128b_warpx4(sf, d_sfp + so);
+        tc::cp_32x128b_warpx4(sf + 4, d_sfp + so + 32);
+        tc::mma_mxf4nvf4_c<false>(t_d1t, d_ident0, d_codes + so, id_mx, t_one, sf);
+        tc::mma_mxf4nvf4_c<true>(t_d1t, d_ident1, d_codes + so + 2, id_mx, t_one + 4, sf + 4);
         mbar_arrive(&sm.bar_t);  // publishes the ring entry to the w warps
-        tc::commit(&sm.bar_t);
+        tc::commit_at(b_t);
       }
       __syncwarp();
       return true;
@@ -470,27 +485,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     ok = front(0, more);
     int n = 0;
     for (; ok && more; ++n) {
-      const int s = n % kStages;
+      const uint32_t s = (uint32_t)n & (kStages - 1);
+      const uint32_t par = (uint32_t)n & 1;
       bool more_next = false;
       if (!front(n + 1, more_next)) { ok = false; break; }
       // MMA1(n) + MMA_r1(n) into D1[n & 1] once w(n) is ready and that group released tile n - 2
-      if (!wait_bar(&sm.bar_w[n & 1], (uint32_t)((n >> 1) & 1), abort_flag)) { ok = false; break; }
-      if (n >= 2 && !wait_bar(&sm.bar_q[n & 1], (uint32_t)(((n - 2) >> 1) & 1), abort_flag)) { ok = false; break; }
+      if (!wait_bar(&sm.bar_w[par], (uint32_t)((n >> 1) & 1), abort_flag)) { ok = false; break; }
+      if (n >= 2 && !wait_bar(&sm.bar_q[par], (uint32_t)(((n - 2) >> 1) & 1), abort_flag)) { ok = false; break; }
       tc::fence_after_sync();
       if (lane == 0) {
-        Stage& st = sm.st[s];
-        const int drop = sm.ring[n % kRing].drop;
-        const uint32_t sf = T + kColSF + 8 * (n % 3);
-        const uint32_t d = T + kColD1 + 128 * (n & 1);
-        if (!drop)
-          for (int kt = 0; kt < 2; ++kt)
-            tc::mma_mxf4nvf4(d, desc_codes(st.codes, kt), tc::smem_desc(sm.ident + 4096 * kt, 2048, 128), id_mx,
-                             sf + 4 * kt, T + kColOne + 4 * kt, kt > 0);
-        tc::mma_tf32_ss(d, tc::smem_desc(st.ak, 128, 256), tc::smem_desc(sm.bw[n & 1], 128, 256), id_r1,
-                        drop ? 0u : 1u);
-        mbar_arrive(&sm.bar_d[n & 1]);  // publishes the ring entry to the requantisers
-        tc::commit(&sm.bar_d[n & 1]);
-        tc::commit(&sm.empty[s]);
+        const uint64_t so = s * kStageDesc;
+        const int drop = sm.ring[n & (kRing - 1)].drop;
+        const uint32_t sf = T + kColSF + 8 * (uint32_t)(n % 3);
+        const uint32_t d = T + kColD1 + 128 * par;
+        if (!drop) {
+          tc::mma_mxf4nvf4_c<false>(d, d_codes + so, d_ident0, id_mx, sf, t_one);
+          tc::mma_mxf4nvf4_c<true>(d, d_codes + so + 2, d_ident1, id_mx, sf + 4, t_one + 4);
+        }
+        tc::mma_tf32_ss(d, d_ak + so, par ? d_bw1 : d_bw0, id_r1, drop ? 0u : 1u);
+        mbar_arrive(&sm.bar_d[par]);  // publishes the ring entry to the requantisers
+        tc::commit_at(b_d0 + 8 * par);
+        tc::commit_at(b_empty0 + 8 * s);
       }
       __syncwarp();
       more = more_next;

@@ -95,6 +95,9 @@ struct Misc {
   float al[kC];    // exp(g): one token's decay
   float inv_tab[256];
   float amax[8];
+  float nrm[4][kC];  // q/k L2 norm: sums of squares of each token's k (0, 1) and q (2, 3) halves
+  float dk[kC];      // 1 / |k_s| (with the norm in the kernel)
+  float dq[kC];      // 1 / |q_r|
   uint64_t bar_kq[2];     // k/q stage loaded
   uint64_t bar_v;         // v loaded
   uint64_t bar_p1;        // prep: P1 done
@@ -139,6 +142,7 @@ struct PrefillArgs {
   float q_scale, gden;
   float* debug_y;
   uint32_t* status;
+  int32_t qk_l2norm;  // q and k scaled to unit L2 norm per token and head in the kernel
 };
 
 // The global scale of pool tile pt (slot * HV + head).
@@ -359,6 +363,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         load_gb(a, nx, tid, g_pre, b_pre);
       }
       group_sync(kBarPrep);
+      if (a.qk_l2norm) {
+        // Sum of squares of one token's half-row of k or q (the issuer saw the
+        // stage land before the barrier above).  The 128-byte swizzle only
+        // permutes the 16-byte chunks of a row, so a row's sum reads it as stored.
+        const int box = tid >> 6, r = tid & 63;
+        const uint32_t off = box == 0 ? kStK0 : box == 1 ? kStK1 : box == 2 ? kStQ0 : kStQ1;
+        const uint4* row = reinterpret_cast<const uint4*>(stage + off + 128 * r);
+        float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 w = row[c];
+          const uint32_t ws4[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws4[e]));
+            acc = __ffma2_rn(f, f, acc);
+          }
+        }
+        ms.nrm[box][r] = acc.x + acc.y;
+      }
       float h_de = 0.0f, h_qg = 0.0f, h_gC = 0.0f;
       if (tid < kC) {
         const float G = ms.gw[tid] + (tid >= 32 ? ms.gw[31] : 0.0f);
@@ -384,10 +408,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc::fence_after_sync();
       if (tid < kC) {
+        if (a.qk_l2norm) {
+          // x / sqrt(sum x^2 + 1e-6) of k_s and q_r folded into every product
+          // that reads k or q: A, P (below), -T diag(beta gamma) (through bg),
+          // the state update (through de) and the output (through qg)
+          const float dk = 1.0f / sqrtf((ms.nrm[0][tid] + ms.nrm[1][tid]) + 1e-6f);
+          const float dq = 1.0f / sqrtf((ms.nrm[2][tid] + ms.nrm[3][tid]) + 1e-6f);
+          ms.dk[tid] = dk;
+          ms.dq[tid] = dq;
+          ms.bg[tid] *= dk;
+          h_de *= dk;
+          h_qg *= dq;
+        }
         hd.de[tid] = h_de;
         hd.qg[tid] = h_qg;
         if (tid == 0) hd.gC = h_gC;
       }
+      if (a.qk_l2norm) group_sync(kBarPrep);
       if (tid == kPrepIssuer || tid == kPrepIssuer - 32)
         issue_v_part(a, vbuf, &ms.bar_v, cur, &tm_v, tid == kPrepIssuer ? 0 : 1);
 
@@ -405,7 +442,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = arow ? lrow : lrow - 64;
         const int s_hi = arow ? r - 1 : r;           // last column kept
         const float Gr = ms.G[r];
-        const float scale = arow ? ms.bet[r] : a.q_scale;
+        float scale = arow ? ms.bet[r] : a.q_scale;
+        if (a.qk_l2norm) scale *= arow ? ms.dk[r] : ms.dq[r];
         const int s_top = s_hi < sb0 + 31 ? s_hi : sb0 + 31;
         float f = (s_top >= sb0) ? __expf(Gr - ms.G[s_top]) : 0.0f;
         float alv[33];  // exp(g) of tokens sb0 .. sb0 + 32, in registers before the chain
@@ -423,6 +461,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = sb0 + e;
           if (s < s_top) f *= alv[e + 1];
           vals[e] = (s <= s_top) ? scale * vals[e] * f : 0.0f;
+        }
+        if (a.qk_l2norm) {  // column s: 1 / |k_s|
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4) {
+            const float4 d4 = *reinterpret_cast<const float4*>(ms.dk + sb0 + 4 * c4);
+            vals[4 * c4] *= d4.x;
+            vals[4 * c4 + 1] *= d4.y;
+            vals[4 * c4 + 2] *= d4.z;
+            vals[4 * c4 + 3] *= d4.w;
+          }
         }
         if (arow) {
 #pragma unroll
@@ -941,6 +989,7 @@ extern "C" int gdn_prefill(const gdn_prefill_params* p, cudaStream_t stream) {
   a.debug_y = p->debug_y;
   a.status = device_status_ptr();
   if (!a.status) return GDN_ERR_CUDA;
+  a.qk_l2norm = p->qk_l2norm;
   CUtensorMap tq, tk, tv;
   if (!make_row_map(&tq, p->q, p->num_k_heads, p->total_tokens, q_stride) ||
       !make_row_map(&tk, p->k, p->num_k_heads, p->total_tokens, k_stride) ||

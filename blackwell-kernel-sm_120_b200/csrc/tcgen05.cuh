@@ -112,7 +112,24 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
                : "memory");
 }
 
+// As commit, for an mbarrier given by its shared-memory address.
+__device__ __forceinline__ void commit_at(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 // ---- MMAs (single thread) ----------------------------------------------------------------
+
+// As mma_mxf4nvf4 with the accumulate flag known at compile time.
+template <bool kAccumulate>
+__device__ __forceinline__ void mma_mxf4nvf4_c(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t sfa_tmem, uint32_t sfb_tmem) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %6, 0;\n"
+      "  tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%4], [%5], p; }" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "n"(kAccumulate ? 1 : 0)
+      : "memory");
+}
 
 __device__ __forceinline__ void mma_mxf4nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                              uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {

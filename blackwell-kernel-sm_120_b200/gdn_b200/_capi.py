@@ -86,6 +86,7 @@ class PrefillParams(ctypes.Structure):
         ("q_scale", _f32), ("scale_mode", _i32), ("gscale_den", _f32),
         ("debug_y", _p),
         ("pool_tile_stride", _i64),
+        ("qk_l2norm", _i32),
     ]
 
 

@@ -238,13 +238,14 @@ def decode(q, k, v, g, beta, slot_idx, pool, out=None, q_scale: float = 0.0, deb
 
 
 def prefill(q, k, v, g, beta, cu_seqlens, pool=None, slot_idx=None, has_initial_state=None, out=None,
-            q_scale: float = 0.0, debug_y=None):
+            q_scale: float = 0.0, debug_y=None, qk_l2norm: bool = False):
     """Chunked gated-delta-rule prefill of packed variable-length sequences.
     q, k: [T, HK, D] bf16; v: [T, HV, D] bf16; g, beta: [T, HV] fp32;
     cu_seqlens: [N + 1] int32 (CUDA).  With `pool` and `slot_idx` ([N] int32),
     sequence n starts from the pool state at slot_idx[n] when
     has_initial_state[n] (bool [N]) is set, from zero otherwise, and its final
-    state is written back to that slot.  Returns out [T, HV, D] bf16."""
+    state is written back to that slot.  qk_l2norm scales q and k to unit L2
+    norm per token and head inside the kernel.  Returns out [T, HV, D] bf16."""
     T, HK, D = q.shape
     HV = v.shape[1]
     for t, name in ((q, "q"), (k, "k"), (v, "v")):
@@ -289,6 +290,7 @@ def prefill(q, k, v, g, beta, cu_seqlens, pool=None, slot_idx=None, has_initial_
     p.out = out.data_ptr()
     p.q_scale = q_scale
     p.debug_y = _ptr(debug_y)
+    p.qk_l2norm = 1 if qk_l2norm else 0
     check("gdn_prefill", lib.gdn_prefill(ctypes.byref(p), _stream(q)))
     return out
 

@@ -102,11 +102,9 @@ def chunk_gated_delta_rule(q, k, v, g, beta, initial_state, output_final_state: 
     dense [N, HV, V, K].  Returns (o [1, T, HV, D], final_state)."""
     if q.dim() != 4 or q.shape[0] != 1:
         raise ValueError("expected packed varlen inputs of shape [1, T, H, D]")
-    qs, ks, vs = q[0], k[0], v[0]
-    if use_qk_l2norm_in_kernel:
-        qs = l2norm(qs)
-        ks = l2norm(ks)
-    qs, ks, vs = (t.to(torch.bfloat16).contiguous() for t in (qs, ks, vs))
+    # the q/k L2 norm (use_qk_l2norm_in_kernel) runs inside the prefill kernel
+    qs, ks, vs = (t.to(torch.bfloat16).contiguous() for t in (q[0], k[0], v[0]))
+    l2 = bool(use_qk_l2norm_in_kernel)
     T = qs.shape[0]
     if cu_seqlens is None:
         cu_seqlens = torch.tensor([0, T], dtype=torch.int32, device=q.device)
@@ -123,12 +121,12 @@ def chunk_gated_delta_rule(q, k, v, g, beta, initial_state, output_final_state: 
         pool = NVFP4StatePool.records(recs, scale_mode)
         slot = torch.arange(N, dtype=torch.int32, device=q.device)
         o = ops.prefill(qs, ks, vs, gs, bs, cu, pool=pool, slot_idx=slot,
-                        has_initial_state=torch.ones(N, dtype=torch.bool, device=q.device))
+                        has_initial_state=torch.ones(N, dtype=torch.bool, device=q.device), qk_l2norm=l2)
         final = recs
     elif initial_state is not None and initial_state.dtype == torch.uint8:
         # vLLM's kernel warm-up builds a zero [1, HV, V, K] state of the cache
         # dtype: a zero initial state, nothing to keep
-        o = ops.prefill(qs, ks, vs, gs, bs, cu)
+        o = ops.prefill(qs, ks, vs, gs, bs, cu, qk_l2norm=l2)
         final = initial_state
     else:
         pool = slot = has = None
@@ -139,7 +137,7 @@ def chunk_gated_delta_rule(q, k, v, g, beta, initial_state, output_final_state: 
             else:
                 pool = NVFP4StatePool.zeros(N, HV, D, q.device, scale_mode=scale_mode)
             slot = torch.arange(N, dtype=torch.int32, device=q.device)
-        o = ops.prefill(qs, ks, vs, gs, bs, cu, pool=pool, slot_idx=slot, has_initial_state=has)
+        o = ops.prefill(qs, ks, vs, gs, bs, cu, pool=pool, slot_idx=slot, has_initial_state=has, qk_l2norm=l2)
         if output_final_state:
             final = _from_pool(pool, initial_state.dtype if initial_state is not None else torch.float32)
     o = o.unsqueeze(0)

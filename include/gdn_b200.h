@@ -241,6 +241,8 @@ typedef struct gdn_prefill_params {
   float gscale_den;       /* <= 0 selects 6*saturation */
   float* debug_y;         /* optional [N, HV, D, D]: fp32 quantiser inputs of the final states */
   int64_t pool_tile_stride; /* pool layout, as in gdn_decode_params (0: dense arrays) */
+  int32_t qk_l2norm;      /* != 0: q and k scaled to unit L2 norm per token and head, x / sqrt(sum x^2 + 1e-6),
+                             in fp32 inside the kernel (vLLM's use_qk_l2norm_in_kernel) */
 } gdn_prefill_params;
 
 GDN_API int gdn_prefill(const gdn_prefill_params* params, cudaStream_t stream);

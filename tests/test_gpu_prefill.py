@@ -243,3 +243,41 @@ def test_prefill_long_sequence(cuda):
         ref, _ = ob.recurrent_f64(np.zeros((D, D)), q[:, hk], k[:, hk], v[:, h], g[:, h], be[:, h], QS)
         rel = np.linalg.norm(on[:, h] - ref) / np.linalg.norm(ref)
         assert rel <= O_NORM_TOL, (h, rel)
+
+
+def test_prefill_qk_l2norm_in_kernel(cuda):
+    """qk_l2norm: q and k arrive unnormalised (each token scaled by 0.3 .. 3)
+    and the kernel scales them to unit L2 norm, x / sqrt(sum x^2 + 1e-6) in
+    fp32 (vLLM's use_qk_l2norm_in_kernel).  Outputs and final states follow
+    the f64 recurrence of the normalised q, k; from a pool state too."""
+    from gdn_b200 import ops
+    lengths = [1, 70, 130, 64]
+    x, cu = _inputs(lengths, seed=33)
+    gen = torch.Generator().manual_seed(34)
+    T = int(cu[-1])
+    sq = (0.3 + 2.7 * torch.rand((T, HK, 1), generator=gen)).cuda()
+    sk = (0.3 + 2.7 * torch.rand((T, HK, 1), generator=gen)).cuda()
+    raw = dict(x, q=(x["q"].float() * sq).to(torch.bfloat16), k=(x["k"].float() * sk).to(torch.bfloat16))
+    # the reference: the raw bf16 rows normalised in fp32
+    ref_in = dict(x)
+    for n in ("q", "k"):
+        f = raw[n].float()
+        ref_in[n] = f / torch.sqrt((f * f).sum(-1, keepdim=True) + 1e-6)
+    pool = _pool(len(lengths), 1, seed=35)
+    S0 = pool.dequantize().cpu().numpy()
+    slots = list(range(len(lengths)))
+    cu_t = torch.from_numpy(cu).cuda()
+    o = ops.prefill(raw["q"], raw["k"], raw["v"], raw["g"], raw["beta"], cu_t, pool=pool,
+                    slot_idx=torch.tensor(slots, dtype=torch.int32, device="cuda"),
+                    has_initial_state=torch.ones(len(lengths), dtype=torch.bool, device="cuda"), qk_l2norm=True)
+    torch.cuda.synchronize()
+    o_ref, S_ref = _reference(ref_in, cu, S0)
+    print("qk_l2norm worst (norm, max):", _check_outputs(o, o_ref, cu))
+    S = pool.dequantize().cpu().numpy()
+    for n in range(len(lengths)):
+        for h in range(0, HV, 5):
+            # the final state crosses NVFP4 once: the requantisation error dominates
+            assert np.linalg.norm(S[n, h] - S_ref[n, h]) <= 0.15 * np.linalg.norm(S_ref[n, h])
+    # without the flag the same raw inputs give a different result
+    o_raw = ops.prefill(raw["q"], raw["k"], raw["v"], raw["g"], raw["beta"], cu_t)
+    assert not torch.equal(o_raw, o)
