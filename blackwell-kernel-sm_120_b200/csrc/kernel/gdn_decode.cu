@@ -31,14 +31,15 @@
 // by one 2-D TMA copy with 64-byte swizzle that both decode MMAs read in
 // place.
 //
-// Warp roles (one CTA per SM, 27 warps):
+// Warp roles (one CTA per SM, 28 warps):
 //   warp 25     producer: walks the CTA's tiles, loads the per-tile scalars
 //               into a metadata ring, queues the TMA copies into an 8-stage
 //               ring, zeroes the outputs of padding tiles;
 //   warp 26     staging: once a stage lands, permutes its scale factors into
 //               the tcgen05.cp layout and writes the fp32 k / q operands;
-//   warp 24     MMA: only tcgen05 work -- every copy, MMA and commit; it
-//               issues tile n+1's MMA1' before tile n's update;
+//   warp 24     MMA front: tile n's scale-factor copies and MMA1';
+//   warp 27     MMA back: tile n's MMA1 and rank-1 update (the two issue in
+//               parallel: a tcgen05 operation takes ~65-140 cycles to issue);
 //   warps 16-23 w: u, p -> w, o (stored) and the rank-1 operand;
 //   warps 0-15  requantisers, two groups of 8 taking alternate tiles.
 // Every wait is bounded; a timeout in any role stops all of them.
@@ -58,10 +59,11 @@ namespace {
 
 constexpr int kD = 128;
 constexpr int kWWarp0 = 16;  // 8 w warps
-constexpr int kMmaWarp = 24;
+constexpr int kMmaWarp = 24;      // issues the scale-factor copies and MMA1'
 constexpr int kProdWarp = 25;
 constexpr int kStageWarp = 26;
-constexpr int kThreads = 27 * 32;
+constexpr int kMmaBackWarp = 27;  // issues MMA1 and the rank-1 update
+constexpr int kThreads = 28 * 32;
 constexpr int kStages = 8;
 constexpr int kRing = 16;  // metadata ring entries
 constexpr uint32_t kCodeBytes = kD * kD / 2;    // 8192
@@ -118,7 +120,7 @@ struct __align__(1024) DecodeSmem {
   float inv_tab[256];
   uint32_t rtab[8];             // scale_inv_w's reciprocal significands
   uint64_t full[kStages], ready[kStages], empty[kStages];
-  uint64_t bar_t, bar_tfree, bar_w[2], bar_d[2], bar_q[2], bar_fin;
+  uint64_t bar_t, bar_tfree, bar_w[2], bar_d[2], bar_q[2], bar_fin[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -240,7 +242,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.bar_q[b], 8);
       sm.amax_bits[b][0] = sm.amax_bits[b][1] = 0u;
     }
-    mbar_init(&sm.bar_fin, 1);
+    mbar_init(&sm.bar_fin[0], 1);
+    mbar_init(&sm.bar_fin[1], 1);
     sm.abort_flag = 0;
     fence_mbar_init();
   }
@@ -437,13 +440,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&sm.ready[s]);  // publishes sfp, kq4, ak and m.kq
       if (m.end) break;
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == kMmaWarp || warp == kMmaBackWarp) {
     // ===================================== MMA =====================================
+    // Two issuing warps, since one tcgen05 operation takes ~65-140 cycles to
+    // issue: the front warp copies tile n's scale factors to TMEM and decodes
+    // D1' = I S_dq^T; the back warp decodes D1 = S_dq I and adds the rank-1
+    // update once the w warps have formed it.  Operations of different threads
+    // are not ordered with each other, so each side waits for what the other
+    // issued through barriers it already shares with the other roles:
+    //   * the back warp's MMA1(n) reads scale-factor slot n % 3 and the stage
+    //     after the w warps arrived on bar_w(n), which they do after bar_t(n),
+    //     the commit of the front warp's copies and MMA1'(n);
+    //   * the front warp rewrites slot n % 3 for tile n + 3 after empty(n),
+    //     the back warp's commit of tile n's last MMA (a stage's empty barrier
+    //     completes once per use, so its phase cannot run ahead).
     // Every shared-memory descriptor, TMEM address and mbarrier address is
     // formed once here: a stage's descriptors are the first stage's plus the
-    // stage offset (the start-address field holds address >> 4), so issuing a
-    // tcgen05 operation costs a few instructions instead of a chain of 64-bit
-    // address arithmetic on the critical path.
+    // stage offset (the start-address field holds address >> 4).
+    const bool front_warp = warp == kMmaWarp;
     const uint32_t id_mx = tc::idesc_mxf4nvf4(128, 128);
     const uint32_t id_r1 = tc::idesc_tf32(128, 128);
     constexpr uint32_t kStageDesc = sizeof(Stage) >> 4;
@@ -456,81 +470,90 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t d_bw1 = tc::smem_desc(sm.bw[1], 128, 256);
     const uint32_t t_one = T + kColOne, t_d1t = T + kColD1t;
     const uint32_t b_t = smem_u32(&sm.bar_t), b_d0 = smem_u32(&sm.bar_d[0]), b_empty0 = smem_u32(&sm.empty[0]);
-    if (lane == 0)
+    if (front_warp && lane == 0)
       for (int kt = 0; kt < 2; ++kt) tc::cp_32x128b_warpx4(t_one + 4 * kt, tc::smem_desc(sm.sf_one + 512 * kt, 0, 128));
     bool ok = true;
-    // Tile n: scale factors to TMEM and MMA1' into D1' (free: the w warps
-    // loaded tile n - 1's).
-    auto front = [&](int n, bool& more) -> bool {
-      const uint32_t s = (uint32_t)n & (kStages - 1);
-      if (!wait_bar(&sm.ready[s], (uint32_t)((n / kStages) & 1), abort_flag)) return false;
-      more = !sm.ring[n & (kRing - 1)].end;
-      if (!more) return true;
-      if (n >= 1 && !wait_bar(&sm.bar_tfree, (uint32_t)((n - 1) & 1), abort_flag)) return false;
-      tc::fence_after_sync();
-      if (lane == 0) {
-        const uint64_t so = s * kStageDesc;
-        const uint32_t sf = T + kColSF + 8 * (uint32_t)(n % 3);
-        tc::cp_32x128b_warpx4(sf, d_sfp + so);
-        tc::cp_32x128b_warpx4(sf + 4, d_sfp + so + 32);
-        tc::mma_mxf4nvf4_c<false>(t_d1t, d_ident0, d_codes + so, id_mx, t_one, sf);
-        tc::mma_mxf4nvf4_c<true>(t_d1t, d_ident1, d_codes + so + 2, id_mx, t_one + 4, sf + 4);
-        mbar_arrive(&sm.bar_t);  // publishes the ring entry to the w warps
-        tc::commit_at(b_t);
-      }
-      __syncwarp();
-      return true;
-    };
-    bool more = true;
-    ok = front(0, more);
     int n = 0;
-    for (; ok && more; ++n) {
-      const uint32_t s = (uint32_t)n & (kStages - 1);
-      const uint32_t par = (uint32_t)n & 1;
-      bool more_next = false;
-      if (!front(n + 1, more_next)) { ok = false; break; }
-      // MMA1(n) + MMA_r1(n) into D1[n & 1] once w(n) is ready and that group released tile n - 2
-      if (!wait_bar(&sm.bar_w[par], (uint32_t)((n >> 1) & 1), abort_flag)) { ok = false; break; }
-      if (n >= 2 && !wait_bar(&sm.bar_q[par], (uint32_t)(((n - 2) >> 1) & 1), abort_flag)) { ok = false; break; }
-      tc::fence_after_sync();
-      if (lane == 0) {
-        const uint64_t so = s * kStageDesc;
-        const int drop = sm.ring[n & (kRing - 1)].drop;
-        const uint32_t sf = T + kColSF + 8 * (uint32_t)(n % 3);
-        const uint32_t d = T + kColD1 + 128 * par;
-        if (!drop) {
-          tc::mma_mxf4nvf4_c<false>(d, d_codes + so, d_ident0, id_mx, sf, t_one);
-          tc::mma_mxf4nvf4_c<true>(d, d_codes + so + 2, d_ident1, id_mx, sf + 4, t_one + 4);
+    if (front_warp) {
+      for (;; ++n) {
+        const uint32_t s = (uint32_t)n & (kStages - 1);
+        if (!wait_bar(&sm.ready[s], (uint32_t)((n / kStages) & 1), abort_flag)) { ok = false; break; }
+        if (sm.ring[n & (kRing - 1)].end) {
+          // The end marker's two arrivals on bar_t must fall in the next phase:
+          // wait until the w warps have read tile n - 1's D1' (so that phase,
+          // closed by the commit of its MMA1', is complete).
+          if (n >= 1 && !wait_bar(&sm.bar_tfree, (uint32_t)((n - 1) & 1), abort_flag)) { ok = false; break; }
+          if (lane == 0) {  // the w warps read ring[n] (the producer's end marker)
+            mbar_arrive(&sm.bar_t);
+            mbar_arrive(&sm.bar_t);
+          }
+          break;
         }
-        tc::mma_tf32_ss(d, d_ak + so, par ? d_bw1 : d_bw0, id_r1, drop ? 0u : 1u);
-        mbar_arrive(&sm.bar_d[par]);  // publishes the ring entry to the requantisers
-        tc::commit_at(b_d0 + 8 * par);
-        tc::commit_at(b_empty0 + 8 * s);
+        // D1' is free once the w warps loaded tile n - 1's; the scale-factor
+        // slot once tile n - 3's MMA1 is complete
+        if (n >= 1 && !wait_bar(&sm.bar_tfree, (uint32_t)((n - 1) & 1), abort_flag)) { ok = false; break; }
+        if (n >= 3 && !wait_bar(&sm.empty[(n - 3) & (kStages - 1)], (uint32_t)(((n - 3) / kStages) & 1), abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        if (lane == 0) {
+          const uint64_t so = s * kStageDesc;
+          const uint32_t sf = T + kColSF + 8 * (uint32_t)(n % 3);
+          tc::cp_32x128b_warpx4(sf, d_sfp + so);
+          tc::cp_32x128b_warpx4(sf + 4, d_sfp + so + 32);
+          tc::mma_mxf4nvf4_c<false>(t_d1t, d_ident0, d_codes + so, id_mx, t_one, sf);
+          tc::mma_mxf4nvf4_c<true>(t_d1t, d_ident1, d_codes + so + 2, id_mx, t_one + 4, sf + 4);
+          mbar_arrive(&sm.bar_t);  // publishes the ring entry to the w warps
+          tc::commit_at(b_t);
+        }
+        __syncwarp();
       }
-      __syncwarp();
-      more = more_next;
-    }
-    // end: release the w warps and both requantiser groups into end markers
-    if (ok) {
-      const int N = n;
-      if (lane == 0) {  // the w warps read ring[N] (the producer's end marker)
-        mbar_arrive(&sm.bar_t);
-        mbar_arrive(&sm.bar_t);
+    } else {
+      for (;; ++n) {
+        const uint32_t s = (uint32_t)n & (kStages - 1);
+        const uint32_t par = (uint32_t)n & 1;
+        if (!wait_bar(&sm.ready[s], (uint32_t)((n / kStages) & 1), abort_flag)) { ok = false; break; }
+        if (sm.ring[n & (kRing - 1)].end) break;
+        // MMA1(n) + MMA_r1(n) into D1[n & 1] once w(n) is ready and that group released tile n - 2
+        if (!wait_bar(&sm.bar_w[par], (uint32_t)((n >> 1) & 1), abort_flag)) { ok = false; break; }
+        if (n >= 2 && !wait_bar(&sm.bar_q[par], (uint32_t)(((n - 2) >> 1) & 1), abort_flag)) { ok = false; break; }
+        tc::fence_after_sync();
+        if (lane == 0) {
+          const uint64_t so = s * kStageDesc;
+          const int drop = sm.ring[n & (kRing - 1)].drop;
+          const uint32_t sf = T + kColSF + 8 * (uint32_t)(n % 3);
+          const uint32_t d = T + kColD1 + 128 * par;
+          if (!drop) {
+            tc::mma_mxf4nvf4_c<false>(d, d_codes + so, d_ident0, id_mx, sf, t_one);
+            tc::mma_mxf4nvf4_c<true>(d, d_codes + so + 2, d_ident1, id_mx, sf + 4, t_one + 4);
+          }
+          tc::mma_tf32_ss(d, d_ak + so, par ? d_bw1 : d_bw0, id_r1, drop ? 0u : 1u);
+          mbar_arrive(&sm.bar_d[par]);  // publishes the ring entry to the requantisers
+          tc::commit_at(b_d0 + 8 * par);
+          tc::commit_at(b_empty0 + 8 * s);
+        }
+        __syncwarp();
       }
-      for (int e = N; ok && e < N + 2; ++e) {  // group e & 1 reads ring[e]
-        if (e >= 2) ok = wait_bar(&sm.bar_q[e & 1], (uint32_t)(((e - 2) >> 1) & 1), abort_flag);
-        if (ok && lane == 0) {
-          sm.ring[e % kRing].end = 1;
-          mbar_arrive(&sm.bar_d[e & 1]);
-          mbar_arrive(&sm.bar_d[e & 1]);
+      // end: release both requantiser groups into end markers
+      if (ok) {
+        const int N = n;
+        for (int e = N; ok && e < N + 2; ++e) {  // group e & 1 reads ring[e]
+          if (e >= 2) ok = wait_bar(&sm.bar_q[e & 1], (uint32_t)(((e - 2) >> 1) & 1), abort_flag);
+          if (ok && lane == 0) {
+            sm.ring[e % kRing].end = 1;
+            mbar_arrive(&sm.bar_d[e & 1]);
+            mbar_arrive(&sm.bar_d[e & 1]);
+          }
         }
       }
     }
     if (!ok) *abort_flag = 1;
     // every tcgen05 operation this warp issued has completed before TMEM is freed
     if (lane == 0) {
-      tc::commit(&sm.bar_fin);
-      mbar_wait_bounded(&sm.bar_fin, 0, kWaitTimeoutNs / 4);
+      uint64_t* fin = &sm.bar_fin[front_warp ? 0 : 1];
+      tc::commit(fin);
+      mbar_wait_bounded(fin, 0, kWaitTimeoutNs / 4);
     }
     __syncwarp();
   } else if (warp >= kWWarp0) {
@@ -559,7 +582,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     for (int n = 0;; ++n) {
       // one thread waits; the others sleep on the group's hardware barrier
-      if (tid == 32 * kWWarp0) wait_bar(&sm.bar_t, (uint32_t)(n & 1), abort_flag);
+      if (tid == 32 * kWWarp0) {
+        wait_bar(&sm.bar_t, (uint32_t)(n & 1), abort_flag);
+        // bw[n & 1] is free once tile n - 2's rank-1 MMA (issued by the back
+        // MMA warp, unordered with the front warp's MMA1') has completed
+        if (n >= 2) wait_bar(&sm.bar_d[n & 1], (uint32_t)(((n - 2) >> 1) & 1), abort_flag);
+      }
       named_bar(kBarW, 256);
       if (*abort_flag) break;
       flush_norm(n - 1);
@@ -712,28 +740,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         uint32_t words[4];
         if (fast) {
+          // both blocks as normal, unclamped scale bytes: RN(y inv) = RN(D1 scale_inv_w)
+          uint32_t fix = 0;
 #pragma unroll
           for (int b = 0; b < 2; ++b) {
             const int bi = 2 * bp + b;
             const uint32_t fin = ws[bi] + 8u * (uint32_t)k - 960u;
-            uint32_t sc;
-            if (fin - 8u <= kSat - 8u) {
-              // a normal, unclamped scale byte: RN(y inv) = RN(D1 scale_inv_w)
-              const float inv0 = scale_inv_w(ws[bi], sm.rtab);
-              const float2 inv2 = make_float2(inv0, inv0);
-              words[2 * b] = e2m1_encode8(x + 8 * b, inv2);
-              words[2 * b + 1] = e2m1_encode8(x + 8 * b + 4, inv2);
-              sc = fin;
-            } else {
-              // a zero, subnormal-scale, saturated or NaN block: the exact path on y = D1 2^k
-              const float a1[1] = {am[bi]};
-              uint32_t w2[2];
-              requant_blocks<kMode, 1>(*reinterpret_cast<const float2(*)[8]>(x + 8 * b), a1, mult, sm.inv_tab, w2,
-                                       sc, nullptr);
-              words[2 * b] = w2[0];
-              words[2 * b + 1] = w2[1];
+            fix |= (fin - 8u > kSat - 8u) ? (1u << b) : 0u;
+            const float inv0 = scale_inv_w(ws[bi], sm.rtab);
+            const float2 inv2 = make_float2(inv0, inv0);
+            words[2 * b] = e2m1_encode8(x + 8 * b, inv2);
+            words[2 * b + 1] = e2m1_encode8(x + 8 * b + 4, inv2);
+            scw |= (fin & 0xFFu) << (8 * bi);
+          }
+          // rare: a zero, subnormal-scale, saturated or NaN block takes the exact
+          // path on y = D1 2^k (one warp-uniform test per pair of blocks)
+          if (__any_sync(0xffffffffu, fix != 0)) {
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+              if (fix & (1u << b)) {
+                const int bi = 2 * bp + b;
+                const float a1[1] = {am[bi]};
+                uint32_t w2[2], sc;
+                requant_blocks<kMode, 1>(*reinterpret_cast<const float2(*)[8]>(x + 8 * b), a1, mult, sm.inv_tab, w2,
+                                         sc, nullptr);
+                words[2 * b] = w2[0];
+                words[2 * b + 1] = w2[1];
+                scw = (scw & ~(0xFFu << (8 * bi))) | (sc << (8 * bi));
+              }
             }
-            scw |= sc << (8 * bi);
           }
         } else {
           const float a2[2] = {am[2 * bp], am[2 * bp + 1]};
