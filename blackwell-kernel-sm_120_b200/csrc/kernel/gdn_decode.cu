@@ -40,8 +40,12 @@
 //   warp 24     MMA front: tile n's scale-factor copies and MMA1';
 //   warp 27     MMA back: tile n's MMA1 and rank-1 update (the two issue in
 //               parallel: a tcgen05 operation takes ~65-140 cycles to issue);
-//   warps 16-23 w: u, p -> w, o (stored) and the rank-1 operand;
-//   warps 0-15  requantisers, two groups of 8 taking alternate tiles.
+//   warps 0-23  three worker groups of 8 warps; group g takes the tiles
+//               n = g (mod 3) and owns one 128-column TMEM buffer X_g, which
+//               holds first D1'(n) (phase A: u, p -> w, o and the rank-1
+//               operand) and then D1(n) (phase B: the requantiser).  Three
+//               tiles are in flight, and no tile waits for another tile's
+//               buffer to be read.
 // Every wait is bounded; a timeout in any role stops all of them.
 #include <cstdint>
 #include <mutex>
@@ -58,7 +62,7 @@ namespace gdn {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kWWarp0 = 16;  // 8 w warps
+constexpr int kGroups = 3;        // worker groups of 8 warps: warps 0-23
 constexpr int kMmaWarp = 24;      // issues the scale-factor copies and MMA1'
 constexpr int kProdWarp = 25;
 constexpr int kStageWarp = 26;
@@ -74,16 +78,16 @@ constexpr float kDropBelow = 1e-30f;            // alpha * gs below this: the de
 constexpr float kIdentInv = 128.0f;             // 1 / (the identity's value 0.5 x its scale 2^-6)
 constexpr int kMaxShift = 100;                  // the fast requantiser path takes 0 <= k <= kMaxShift
 
-// Named hardware barriers (0 is __syncthreads)
-constexpr int kBarQ0 = 1, kBarQ1 = 3, kBarW = 2;
+// Named hardware barriers (0 is __syncthreads): group g uses kBarG0 + g
+constexpr int kBarG0 = 1;
 
 // TMEM columns (512 allocated)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColD1 = 0;     // 2 x 128: D1 (lane i), one per requantiser group
-constexpr uint32_t kColD1t = 256;  // 128: D1' (lane j)
-constexpr uint32_t kColSF = 384;   // 3 x 8: the tile's scale factors (tile n uses n % 3: the
-                                   // slot is rewritten only after tile n - 3's MMA1 is known complete)
-constexpr uint32_t kColOne = 408;  // 8: the identity's scale factors (UE4M3 2^-6)
+constexpr uint32_t kColX = 0;      // 3 x 128: X_g, D1'(n) (lane j) then D1(n) (lane i) of group g's tile
+constexpr uint32_t kColSF = 384;   // 4 x 8: the tile's scale factors (tile n uses n % 4: the
+                                   // slot is rewritten only after tile n - 4's MMA1 is known complete)
+constexpr uint32_t kColOne = 416;  // 8: the identity's scale factors (UE4M3 2^-6)
+constexpr int kSfSlots = 4;
 
 struct TileMeta {
   int64_t pt;       // slot * HV + h
@@ -112,15 +116,17 @@ struct __align__(1024) DecodeSmem {
   Stage st[kStages];
   uint8_t ident[kCodeBytes];  // identity (E2M1 0.5), no-swizzle K-major: byte b of row r at (b % 16) + 16 r + 2048 (b / 16)
   uint8_t sf_one[kScaleBytes];  // the identity's scale factors, UE4M3 2^-6
-  uint8_t bw[2][kD * 8 * 4];    // [128][8] fp32 K-major: columns 0, 1 = hi, lo of w / c
-  float2 red[kD];               // partial [u p] / c of the second half of each row of D1'
-  TileMeta ring[kRing];         // metadata of valid tile n at n % kRing
-  uint32_t amax_bits[2][2];     // per group, per tile parity: tile max |D1| as float bits
-  float nrm[2][4];              // fused norm: per tile parity, per output warp, sum of x^2
+  uint8_t bw[kGroups][kD * 8 * 4];  // per group, [128][8] fp32 K-major: columns 0, 1 = hi, lo of w / c
+  float2 red[kGroups][kD];          // per group, partial [u p] / c of the second half of each row of D1'
+  TileMeta ring[kRing];             // metadata of valid tile n at n % kRing
+  uint32_t amax_bits[kGroups][2];   // per group, per tile parity: tile max |D1| as float bits
+  float nrm[kGroups][4];            // fused norm: per group, per output warp, sum of x^2
   float inv_tab[256];
-  uint32_t rtab[8];             // scale_inv_w's reciprocal significands
+  uint32_t rtab[8];                 // scale_inv_w's reciprocal significands
   uint64_t full[kStages], ready[kStages], empty[kStages];
-  uint64_t bar_t, bar_tfree, bar_w[2], bar_d[2], bar_q[2], bar_fin[2];
+  // per group: bar_t D1' in X_g (MMA1' committed), bar_w w formed (D1' read), bar_d D1 in
+  // X_g (MMA1 and the rank-1 update committed), bar_x X_g free (D1 read)
+  uint64_t bar_t[kGroups], bar_w[kGroups], bar_d[kGroups], bar_x[kGroups], bar_fin[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -136,6 +142,17 @@ __device__ __forceinline__ uint64_t desc_codes(const uint8_t* codes, int kstep) 
 }
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+// Named barrier that also ORs `flag` over the participating threads: every
+// thread gets the same answer, so a group leaves its loop together.
+__device__ __forceinline__ bool named_bar_or(int id, int nthreads, int flag) {
+  uint32_t r;
+  asm volatile(
+      "{ .reg .pred p, q; setp.ne.s32 q, %1, 0; bar.red.or.pred p, %2, %3, q; selp.u32 %0, 1, 0, p; }"
+      : "=r"(r)
+      : "r"(flag), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
 }
 
 struct DecodeArgs {
@@ -225,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     sm.ident[canon(r, byte)] = val;
   }
   if (tid < 256) reinterpret_cast<uint32_t*>(sm.sf_one)[tid] = 0x08080808u;  // UE4M3 2^-6
-  for (int e = tid; e < 2 * kD * 8; e += kThreads) reinterpret_cast<float*>(sm.bw)[e] = 0.0f;
+  for (int e = tid; e < kGroups * kD * 8; e += kThreads) reinterpret_cast<float*>(sm.bw)[e] = 0.0f;
   for (int e = tid; e < kStages * kD * 8; e += kThreads)
     reinterpret_cast<float*>(sm.st[e / (kD * 8)].ak)[e % (kD * 8)] = 0.0f;
   if (tid == 0) {
@@ -234,13 +251,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.ready[s], 1);
       mbar_init(&sm.empty[s], 1);
     }
-    mbar_init(&sm.bar_t, 2);
-    mbar_init(&sm.bar_tfree, 8);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sm.bar_w[b], 4);   // per tile parity: tile n + 1 may finish before tile n is waited for
-      mbar_init(&sm.bar_d[b], 2);   // per requantiser group
-      mbar_init(&sm.bar_q[b], 8);
-      sm.amax_bits[b][0] = sm.amax_bits[b][1] = 0u;
+    for (int g = 0; g < kGroups; ++g) {
+      mbar_init(&sm.bar_t[g], 2);   // the front warp's arrival + its commit
+      mbar_init(&sm.bar_w[g], 4);   // the group's four output warps
+      mbar_init(&sm.bar_d[g], 2);   // the back warp's arrival + its commit
+      mbar_init(&sm.bar_x[g], 8);   // the group's eight warps
+      sm.amax_bits[g][0] = sm.amax_bits[g][1] = 0u;
     }
     mbar_init(&sm.bar_fin[0], 1);
     mbar_init(&sm.bar_fin[1], 1);
@@ -442,18 +458,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kMmaWarp || warp == kMmaBackWarp) {
     // ===================================== MMA =====================================
-    // Two issuing warps, since one tcgen05 operation takes ~65-140 cycles to
+    // Two issuing warps, since one tcgen05 operation takes ~65-150 cycles to
     // issue: the front warp copies tile n's scale factors to TMEM and decodes
-    // D1' = I S_dq^T; the back warp decodes D1 = S_dq I and adds the rank-1
-    // update once the w warps have formed it.  Operations of different threads
-    // are not ordered with each other, so each side waits for what the other
-    // issued through barriers it already shares with the other roles:
-    //   * the back warp's MMA1(n) reads scale-factor slot n % 3 and the stage
-    //     after the w warps arrived on bar_w(n), which they do after bar_t(n),
-    //     the commit of the front warp's copies and MMA1'(n);
-    //   * the front warp rewrites slot n % 3 for tile n + 3 after empty(n),
+    // D1' = I S_dq^T into the buffer X_g of tile n's group g = n % 3; the back
+    // warp decodes D1 = S_dq I into the same buffer and adds the rank-1 update
+    // once the group has formed w.  Operations of different threads are not
+    // ordered with each other, so each side waits for what the other issued
+    // through barriers it already shares with the other roles:
+    //   * the back warp's MMA1(n) reads scale-factor slot n % 4 and overwrites
+    //     D1'(n) after the group arrived on bar_w(n), which it does after
+    //     bar_t(n), the commit of the front warp's copies and MMA1'(n), and
+    //     after every warp of the group loaded D1'(n);
+    //   * the front warp rewrites slot n % 4 for tile n + 4 after empty(n),
     //     the back warp's commit of tile n's last MMA (a stage's empty barrier
-    //     completes once per use, so its phase cannot run ahead).
+    //     completes once per use, so its phase cannot run ahead), and writes
+    //     D1'(n) into X_g after bar_x(n - 3), the group's last load of
+    //     D1(n - 3).
     // Every shared-memory descriptor, TMEM address and mbarrier address is
     // formed once here: a stage's descriptors are the first stage's plus the
     // stage offset (the start-address field holds address >> 4).
@@ -461,91 +481,109 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t id_mx = tc::idesc_mxf4nvf4(128, 128);
     const uint32_t id_r1 = tc::idesc_tf32(128, 128);
     constexpr uint32_t kStageDesc = sizeof(Stage) >> 4;
+    constexpr uint32_t kBwDesc = sizeof(sm.bw[0]) >> 4;
     const uint64_t d_ident0 = tc::smem_desc(sm.ident, 2048, 128);
     const uint64_t d_ident1 = tc::smem_desc(sm.ident + 4096, 2048, 128);
     const uint64_t d_codes = desc_codes(sm.st[0].codes, 0);  // + 2: the second K step (32 bytes)
     const uint64_t d_sfp = tc::smem_desc(sm.st[0].sfp, 0, 128);  // + 32: the second K step (512 bytes)
     const uint64_t d_ak = tc::smem_desc(sm.st[0].ak, 128, 256);
-    const uint64_t d_bw0 = tc::smem_desc(sm.bw[0], 128, 256);
-    const uint64_t d_bw1 = tc::smem_desc(sm.bw[1], 128, 256);
-    const uint32_t t_one = T + kColOne, t_d1t = T + kColD1t;
-    const uint32_t b_t = smem_u32(&sm.bar_t), b_d0 = smem_u32(&sm.bar_d[0]), b_empty0 = smem_u32(&sm.empty[0]);
+    const uint64_t d_bw = tc::smem_desc(sm.bw[0], 128, 256);  // + g kBwDesc: group g's
+    const uint32_t t_one = T + kColOne;
+    const uint32_t b_t0 = smem_u32(&sm.bar_t[0]), b_d0 = smem_u32(&sm.bar_d[0]), b_empty0 = smem_u32(&sm.empty[0]);
     if (front_warp && lane == 0)
       for (int kt = 0; kt < 2; ++kt) tc::cp_32x128b_warpx4(t_one + 4 * kt, tc::smem_desc(sm.sf_one + 512 * kt, 0, 128));
     bool ok = true;
     int n = 0;
     if (front_warp) {
-      for (;; ++n) {
-        const uint32_t s = (uint32_t)n & (kStages - 1);
-        if (!wait_bar(&sm.ready[s], (uint32_t)((n / kStages) & 1), abort_flag)) { ok = false; break; }
-        if (sm.ring[n & (kRing - 1)].end) {
-          // The end marker's two arrivals on bar_t must fall in the next phase:
-          // wait until the w warps have read tile n - 1's D1' (so that phase,
-          // closed by the commit of its MMA1', is complete).
-          if (n >= 1 && !wait_bar(&sm.bar_tfree, (uint32_t)((n - 1) & 1), abort_flag)) { ok = false; break; }
-          if (lane == 0) {  // the w warps read ring[n] (the producer's end marker)
-            mbar_arrive(&sm.bar_t);
-            mbar_arrive(&sm.bar_t);
-          }
-          break;
+      // Tile t's scale factors are copied as soon as its stage is staged and
+      // slot t % 4 is free, ahead of MMA1'(t), which may wait for its buffer.
+      auto copy_sf = [&](int t) -> int {  // 1: copied, 0: t is the end marker, -1: gave up
+        const uint32_t st_i = (uint32_t)t & (kStages - 1);
+        if (!wait_bar(&sm.ready[st_i], (uint32_t)((t / kStages) & 1), abort_flag)) return -1;
+        if (sm.ring[t & (kRing - 1)].end) return 0;
+        // slot t % 4 was last read by tile t - 4's MMA1
+        if (t >= kSfSlots && !wait_bar(&sm.empty[(t - kSfSlots) & (kStages - 1)],
+                                       (uint32_t)(((t - kSfSlots) / kStages) & 1), abort_flag))
+          return -1;
+        tc::fence_after_sync();
+        if (lane == 0) {
+          const uint64_t so = st_i * kStageDesc;
+          const uint32_t sf = T + kColSF + 8 * (uint32_t)(t & (kSfSlots - 1));
+          tc::cp_32x128b_warpx4(sf, d_sfp + so);
+          tc::cp_32x128b_warpx4(sf + 4, d_sfp + so + 32);
         }
-        // D1' is free once the w warps loaded tile n - 1's; the scale-factor
-        // slot once tile n - 3's MMA1 is complete
-        if (n >= 1 && !wait_bar(&sm.bar_tfree, (uint32_t)((n - 1) & 1), abort_flag)) { ok = false; break; }
-        if (n >= 3 && !wait_bar(&sm.empty[(n - 3) & (kStages - 1)], (uint32_t)(((n - 3) / kStages) & 1), abort_flag)) {
-          ok = false;
+        __syncwarp();
+        return 1;
+      };
+      int r = copy_sf(0);
+      for (; r == 1; ++n) {
+        const int g = n % kGroups;
+        // X_g is free once the group has loaded tile n - 3's D1
+        if (n >= kGroups && !wait_bar(&sm.bar_x[g], (uint32_t)(((n - kGroups) / kGroups) & 1), abort_flag)) {
+          r = -1;
           break;
         }
         tc::fence_after_sync();
         if (lane == 0) {
-          const uint64_t so = s * kStageDesc;
-          const uint32_t sf = T + kColSF + 8 * (uint32_t)(n % 3);
-          tc::cp_32x128b_warpx4(sf, d_sfp + so);
-          tc::cp_32x128b_warpx4(sf + 4, d_sfp + so + 32);
-          tc::mma_mxf4nvf4_c<false>(t_d1t, d_ident0, d_codes + so, id_mx, t_one, sf);
-          tc::mma_mxf4nvf4_c<true>(t_d1t, d_ident1, d_codes + so + 2, id_mx, t_one + 4, sf + 4);
-          mbar_arrive(&sm.bar_t);  // publishes the ring entry to the w warps
-          tc::commit_at(b_t);
+          const uint64_t so = ((uint32_t)n & (kStages - 1)) * kStageDesc;
+          const uint32_t sf = T + kColSF + 8 * (uint32_t)(n & (kSfSlots - 1));
+          const uint32_t x = T + kColX + 128 * (uint32_t)g;
+          tc::mma_mxf4nvf4_c<false>(x, d_ident0, d_codes + so, id_mx, t_one, sf);
+          tc::mma_mxf4nvf4_c<true>(x, d_ident1, d_codes + so + 2, id_mx, t_one + 4, sf + 4);
+          mbar_arrive(&sm.bar_t[g]);  // publishes the ring entry to the group
+          tc::commit_at(b_t0 + 8 * g);
         }
         __syncwarp();
+        r = copy_sf(n + 1);  // on 0 the loop's increment leaves n at the end marker
+      }
+      if (r < 0) {
+        ok = false;
+      } else if (r == 0) {
+        // Release every group into an end marker (tiles n, n + 1, n + 2; the
+        // producer wrote ring[n]).  The two arrivals for tile e may complete
+        // bar_t's next phase only after the group has waited on the phase of
+        // its previous tile e - 3 (else both phases would be complete when it
+        // looks, and its parity wait would miss them): wait until the group has
+        // finished tile e - 3 (bar_x).  Ring entries n + 1 and n + 2 held tiles
+        // n - 15 and n - 14, which every role has finished with.
+        for (int e = n; ok && e < n + kGroups; ++e) {
+          const int g = e % kGroups;
+          if (e >= kGroups && !wait_bar(&sm.bar_x[g], (uint32_t)(((e - kGroups) / kGroups) & 1), abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) {
+            if (e > n) sm.ring[e & (kRing - 1)].end = 1;
+            mbar_arrive(&sm.bar_t[g]);
+            mbar_arrive(&sm.bar_t[g]);
+          }
+          __syncwarp();
+        }
       }
     } else {
       for (;; ++n) {
         const uint32_t s = (uint32_t)n & (kStages - 1);
-        const uint32_t par = (uint32_t)n & 1;
+        const int g = n % kGroups;
         if (!wait_bar(&sm.ready[s], (uint32_t)((n / kStages) & 1), abort_flag)) { ok = false; break; }
         if (sm.ring[n & (kRing - 1)].end) break;
-        // MMA1(n) + MMA_r1(n) into D1[n & 1] once w(n) is ready and that group released tile n - 2
-        if (!wait_bar(&sm.bar_w[par], (uint32_t)((n >> 1) & 1), abort_flag)) { ok = false; break; }
-        if (n >= 2 && !wait_bar(&sm.bar_q[par], (uint32_t)(((n - 2) >> 1) & 1), abort_flag)) { ok = false; break; }
+        // MMA1(n) + MMA_r1(n) into X_g once the group has formed w(n)
+        if (!wait_bar(&sm.bar_w[g], (uint32_t)((n / kGroups) & 1), abort_flag)) { ok = false; break; }
         tc::fence_after_sync();
         if (lane == 0) {
           const uint64_t so = s * kStageDesc;
           const int drop = sm.ring[n & (kRing - 1)].drop;
-          const uint32_t sf = T + kColSF + 8 * (uint32_t)(n % 3);
-          const uint32_t d = T + kColD1 + 128 * par;
+          const uint32_t sf = T + kColSF + 8 * (uint32_t)(n & (kSfSlots - 1));
+          const uint32_t d = T + kColX + 128 * (uint32_t)g;
           if (!drop) {
             tc::mma_mxf4nvf4_c<false>(d, d_codes + so, d_ident0, id_mx, sf, t_one);
             tc::mma_mxf4nvf4_c<true>(d, d_codes + so + 2, d_ident1, id_mx, sf + 4, t_one + 4);
           }
-          tc::mma_tf32_ss(d, d_ak + so, par ? d_bw1 : d_bw0, id_r1, drop ? 0u : 1u);
-          mbar_arrive(&sm.bar_d[par]);  // publishes the ring entry to the requantisers
-          tc::commit_at(b_d0 + 8 * par);
+          tc::mma_tf32_ss(d, d_ak + so, d_bw + (uint64_t)g * kBwDesc, id_r1, drop ? 0u : 1u);
+          mbar_arrive(&sm.bar_d[g]);  // publishes the ring entry to the group's requantiser phase
+          tc::commit_at(b_d0 + 8 * g);
           tc::commit_at(b_empty0 + 8 * s);
         }
         __syncwarp();
-      }
-      // end: release both requantiser groups into end markers
-      if (ok) {
-        const int N = n;
-        for (int e = N; ok && e < N + 2; ++e) {  // group e & 1 reads ring[e]
-          if (e >= 2) ok = wait_bar(&sm.bar_q[e & 1], (uint32_t)(((e - 2) >> 1) & 1), abort_flag);
-          if (ok && lane == 0) {
-            sm.ring[e % kRing].end = 1;
-            mbar_arrive(&sm.bar_d[e & 1]);
-            mbar_arrive(&sm.bar_d[e & 1]);
-          }
-        }
       }
     }
     if (!ok) *abort_flag = 1;
@@ -556,123 +594,110 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait_bounded(fin, 0, kWaitTimeoutNs / 4);
     }
     __syncwarp();
-  } else if (warp >= kWWarp0) {
-    // ================================ w and outputs ================================
-    const int quad = warp & 3, half = (warp >> 2) & 1;
-    const int j = 32 * quad + lane;
-    const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
-    const float norm_wj = kNorm ? __ldg(a.norm_weight + j) : 0.0f;
-    // Fused norm: tile n's normed output is stored after tile n + 1's first
-    // barrier, which is also where every half-0 warp's sum of x^2 for tile n is
-    // visible (no barrier of its own): x, z and the row are carried over.
-    float pend_x = 0.0f, pend_z = 0.0f;
-    int64_t pend_row = -1;
-    auto flush_norm = [&](int np) {
-      if (!kNorm || half || pend_row < 0) return;
-      const float* nr = sm.nrm[np & 1];
-      const float r = rsqrtf(((nr[0] + nr[1]) + (nr[2] + nr[3])) * (1.0f / kD) + a.norm_eps);
-      float y = (pend_x * r) * norm_wj;
-      if (a.gate_z) {
-        const float sg = 1.0f / (1.0f + expf(-pend_z));
-        y = y * (a.norm_act ? sg : pend_z * sg);
-      }
-      const float y1 = __shfl_down_sync(0xffffffffu, y, 1);
-      if ((j & 1) == 0) reinterpret_cast<uint32_t*>(a.out + pend_row * kD)[j >> 1] = pack_bf16x2(y, y1);
-      pend_row = -1;
-    };
-    for (int n = 0;; ++n) {
-      // one thread waits; the others sleep on the group's hardware barrier
-      if (tid == 32 * kWWarp0) {
-        wait_bar(&sm.bar_t, (uint32_t)(n & 1), abort_flag);
-        // bw[n & 1] is free once tile n - 2's rank-1 MMA (issued by the back
-        // MMA warp, unordered with the front warp's MMA1') has completed
-        if (n >= 2) wait_bar(&sm.bar_d[n & 1], (uint32_t)(((n - 2) >> 1) & 1), abort_flag);
-      }
-      named_bar(kBarW, 256);
-      if (*abort_flag) break;
-      flush_norm(n - 1);
-      const TileMeta m = sm.ring[n % kRing];
-      if (m.end) break;
-      const Stage& st = sm.st[n % kStages];
-      tc::fence_after_sync();
-      // [u p] / c: this warp's half (64 columns i) of row j of D1', 32 at a time
-      float2 su0 = make_float2(0.0f, 0.0f), sp0 = su0, su1 = su0, sp1 = su0;
-      const uint32_t ta = T + lane_base + kColD1t + 64 * half;
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        float2 x[16];
-        tc::ld_32x32b_x32(ta + 32 * h2, reinterpret_cast<float*>(x));
-        tc::ld_wait();
-        if (h2 == 1) {
-          tc::fence_before_sync();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.bar_tfree);  // D1' is read
-        }
-        const float4* kq4 = st.kq4 + 32 * half + 16 * h2;
-#pragma unroll
-        for (int p = 0; p < 16; p += 2) {
-          const float4 ka = kq4[p], kb = kq4[p + 1];
-          su0 = __ffma2_rn(x[p], make_float2(ka.x, ka.y), su0);
-          sp0 = __ffma2_rn(x[p], make_float2(ka.z, ka.w), sp0);
-          su1 = __ffma2_rn(x[p + 1], make_float2(kb.x, kb.y), su1);
-          sp1 = __ffma2_rn(x[p + 1], make_float2(kb.z, kb.w), sp1);
-        }
-      }
-      const float2 su = __fadd2_rn(su0, su1), sp = __fadd2_rn(sp0, sp1);
-      if (half) sm.red[j] = make_float2(su.x + su.y, sp.x + sp.y);
-      named_bar(kBarW, 256);
-      if (half) continue;
-      const float2 r = sm.red[j];
-      const float c = m.drop ? 0.0f : m.c;
-      const float u = su.x + su.y + r.x, p = sp.x + sp.y + r.y;
-      const float vj = bf2f(st.v[j]);
-      const float wj = m.beta * (vj - c * u);
-      const float o = a.q_scale * fmaf(m.kq, wj, c * p);
-      if (kNorm) {
-        // gated RMS norm over the head: x = the bf16 output; this warp's sum of
-        // x^2 now, x * rsqrt(mean(x^2) + eps) * weight * act(z) after the next barrier
-        pend_x = __bfloat162float(__float2bfloat16_rn(o));
-        pend_z = a.gate_z ? bf2f(st.z[j]) : 0.0f;
-        pend_row = (int64_t)m.b * a.HV + m.h;
-        float sq = pend_x * pend_x;
-#pragma unroll
-        for (int s5 = 16; s5 > 0; s5 >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, s5);
-        if (lane == 0) sm.nrm[n & 1][quad] = sq;
-      } else {
-        const float o1 = __shfl_down_sync(0xffffffffu, o, 1);
-        if ((j & 1) == 0)
-          reinterpret_cast<uint32_t*>(a.out + ((int64_t)m.b * a.HV + m.h) * kD)[j >> 1] =
-              pack_bf16x2(o, o1);  // one paired conversion (faster than two single ones)
-      }
-      const float wc = wj * m.inv_c;
-      const float hi = __uint_as_float(__float_as_uint(wc) & 0xFFFFE000u);
-      uint8_t* bw = sm.bw[n & 1];
-      *reinterpret_cast<float*>(bw + kf32(j, 0, 256)) = hi;
-      *reinterpret_cast<float*>(bw + kf32(j, 1, 256)) = wc - hi;
-      tc::fence_smem_to_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.bar_w[n & 1]);
-    }
   } else {
-    // ================================ requantisation ================================
-    const int grp = warp >> 3;                    // tiles n with n & 1 == grp
+    // ================================ worker groups ================================
+    // Group g = warp / 8 takes the tiles n = g (mod 3).  Its warp w (0-7) reads
+    // lane quadrant w % 4 and column half w / 4 of X_g, so `row` is j (over
+    // d_v) in phase A, where X_g holds D1', and i (over d_k) in phase B, where
+    // it holds D1.
+    const int grp = warp >> 3;
     const int quad = warp & 3, half = (warp >> 2) & 1;
-    const int row = 32 * quad + lane;             // TMEM lane = state row i
+    const int row = 32 * quad + lane;
     const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
-    const int bar_id = grp ? kBarQ1 : kBarQ0;
+    const uint32_t ta = T + lane_base + kColX + 128 * grp + 64 * half;
+    const int bar_id = kBarG0 + grp;
     const int lead = 256 * grp;                   // the group's first thread
     const uint32_t gden_bits = __float_as_uint(a.gden);
     constexpr uint32_t kSat = kMode ? 0x7Eu : 0x77u;
+    const float norm_wj = kNorm ? __ldg(a.norm_weight + row) : 0.0f;
+    uint8_t* const bw = sm.bw[grp];
     for (int l = 0;; ++l) {
-      const int n = 2 * l + grp;
+      const int n = kGroups * l + grp;
+      // ------------- phase A: [u p] / c = D1' [k q], then w, o and the rank-1 operand -------------
       // one thread waits; the others sleep on the group's hardware barrier
-      if (tid == lead) wait_bar(&sm.bar_d[grp], (uint32_t)(l & 1), abort_flag);
-      named_bar(bar_id, 256);
-      if (*abort_flag) break;
+      if (tid == lead) wait_bar(&sm.bar_t[grp], (uint32_t)(l & 1), abort_flag);
+      if (named_bar_or(bar_id, 256, *abort_flag)) break;
       const TileMeta m = sm.ring[n % kRing];
       if (m.end) break;
+      // fused norm: this thread's bf16 output and gate, normed after phase B's
+      // first barrier (where every output warp's sum of x^2 is visible)
+      float pend_x = 0.0f, pend_z = 0.0f;
+      {
+        const Stage& st = sm.st[n % kStages];
+        tc::fence_after_sync();
+        // this warp's half (64 columns i) of row j of D1', 32 at a time
+        float2 su0 = make_float2(0.0f, 0.0f), sp0 = su0, su1 = su0, sp1 = su0;
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          float2 x[16];
+          tc::ld_32x32b_x32(ta + 32 * h2, reinterpret_cast<float*>(x));
+          tc::ld_wait();
+          const float4* kq4 = st.kq4 + 32 * half + 16 * h2;
+#pragma unroll
+          for (int p = 0; p < 16; p += 2) {
+            const float4 ka = kq4[p], kb = kq4[p + 1];
+            su0 = __ffma2_rn(x[p], make_float2(ka.x, ka.y), su0);
+            sp0 = __ffma2_rn(x[p], make_float2(ka.z, ka.w), sp0);
+            su1 = __ffma2_rn(x[p + 1], make_float2(kb.x, kb.y), su1);
+            sp1 = __ffma2_rn(x[p + 1], make_float2(kb.z, kb.w), sp1);
+          }
+        }
+        // D1' is read; the barrier below and bar_w order these loads before
+        // the back warp's MMA1, which overwrites X_g
+        tc::fence_before_sync();
+        const float2 su = __fadd2_rn(su0, su1), sp = __fadd2_rn(sp0, sp1);
+        if (half) sm.red[grp][row] = make_float2(su.x + su.y, sp.x + sp.y);
+        named_bar(bar_id, 256);
+        // bw[grp] is free: its last reader, tile n - 3's rank-1 MMA, completed
+        // before the group's bar_d wait of that tile
+        if (!half) {
+          const int j = row;
+          const float2 r = sm.red[grp][j];
+          const float c = m.drop ? 0.0f : m.c;
+          const float u = su.x + su.y + r.x, p = sp.x + sp.y + r.y;
+          const float vj = bf2f(st.v[j]);
+          const float wj = m.beta * (vj - c * u);
+          const float o = a.q_scale * fmaf(m.kq, wj, c * p);
+          if (kNorm) {
+            // gated RMS norm over the head: x = the bf16 output; this warp's sum of x^2 now
+            pend_x = __bfloat162float(__float2bfloat16_rn(o));
+            pend_z = a.gate_z ? bf2f(st.z[j]) : 0.0f;
+            float sq = pend_x * pend_x;
+#pragma unroll
+            for (int s5 = 16; s5 > 0; s5 >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, s5);
+            if (lane == 0) sm.nrm[grp][quad] = sq;
+          } else {
+            const float o1 = __shfl_down_sync(0xffffffffu, o, 1);
+            if ((j & 1) == 0)
+              reinterpret_cast<uint32_t*>(a.out + ((int64_t)m.b * a.HV + m.h) * kD)[j >> 1] =
+                  pack_bf16x2(o, o1);  // one paired conversion (faster than two single ones)
+          }
+          const float wc = wj * m.inv_c;
+          const float hi = __uint_as_float(__float_as_uint(wc) & 0xFFFFE000u);
+          *reinterpret_cast<float*>(bw + kf32(j, 0, 256)) = hi;
+          *reinterpret_cast<float*>(bw + kf32(j, 1, 256)) = wc - hi;
+          tc::fence_smem_to_async();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.bar_w[grp]);
+        }
+      }
+      // ---------------------------- phase B: requantise D1 ----------------------------
+      if (tid == lead) wait_bar(&sm.bar_d[grp], (uint32_t)(l & 1), abort_flag);
+      if (named_bar_or(bar_id, 256, *abort_flag)) break;
+      if (kNorm && !half) {
+        // x * rsqrt(mean(x^2) + eps) * weight * act(z), vLLM's RMSNormGated (norm before gate)
+        const float* nr = sm.nrm[grp];
+        const float rs = rsqrtf(((nr[0] + nr[1]) + (nr[2] + nr[3])) * (1.0f / kD) + a.norm_eps);
+        float y = (pend_x * rs) * norm_wj;
+        if (a.gate_z) {
+          const float sg = 1.0f / (1.0f + expf(-pend_z));
+          y = y * (a.norm_act ? sg : pend_z * sg);
+        }
+        const float y1 = __shfl_down_sync(0xffffffffu, y, 1);
+        if ((row & 1) == 0)
+          reinterpret_cast<uint32_t*>(a.out + ((int64_t)m.b * a.HV + m.h) * kD)[row >> 1] = pack_bf16x2(y, y1);
+      }
       tc::fence_after_sync();
-      const uint32_t ta = T + lane_base + kColD1 + 128 * grp + 64 * half;
       // pass 1: block maxima of this thread's 64 values, columns 32-63 first (columns
       // 0-31 stay in registers for pass 2), and each block's provisional scale
       float am[4];
@@ -733,10 +758,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           tc::ld_32x32b_x32(ta + 32, reinterpret_cast<float*>(x));
           tc::ld_wait();
-          // D1 is read: release it to the MMA warp
+          // D1 is read: X_g is free for the group's next tile
           tc::fence_before_sync();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.bar_q[grp]);
+          if (lane == 0) mbar_arrive(&sm.bar_x[grp]);
         }
         uint32_t words[4];
         if (fast) {
