@@ -141,7 +141,10 @@ GDN_API int gdn_nvfp4_dequantize_tiles(const uint8_t* codes, const uint8_t* scal
  *   alpha = exp(g);  S_a = alpha*S;  u = S_a^T k;  w = beta*(v - u)
  *   S' = S_a + k w^T;  out = q_scale * S'^T q
  * S is the NVFP4 tile at pool slot slot_idx[b]; S' is written back in place
- * with a fresh global scale.  A negative slot marks padding (out = 0, pool
+ * with a fresh global scale gs' in [A/gscale_den, 2A/gscale_den), A = max |S'|:
+ * a power-of-two multiple of alpha*gs, so that the E2M1 codes of every block
+ * follow from S'/(alpha*gs) alone; codes and scales are those of the reference
+ * quantiser applied to S'/gs'.  A negative slot marks padding (out = 0, pool
  * untouched); a slot >= num_slots is skipped the same way and flagged in the
  * device status.  Non-negative slots must be distinct.  head_dim must be 128. */
 typedef struct gdn_decode_params {
