@@ -702,14 +702,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // 0-31 stay in registers for pass 2), and each block's provisional scale
       float am[4];
       uint32_t ws[4];
-      float tmax = 0.0f;
       float2 x0[16];
       {
         float2 x[16];
         tc::ld_32x32b_x32(ta + 32, reinterpret_cast<float*>(x));
         tc::ld_wait();
         float a2[2];
-        tmax = block_amax3<2>(x, a2);
+        block_amax3_raw<2>(x, a2);
         am[2] = a2[0];
         am[3] = a2[1];
       }
@@ -717,13 +716,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::ld_32x32b_x32(ta, reinterpret_cast<float*>(x0));
         tc::ld_wait();
         float a2[2];
-        tmax = fmaxf(tmax, block_amax3<2>(x0, a2));
+        block_amax3_raw<2>(x0, a2);
         am[0] = a2[0];
         am[1] = a2[1];
       }
+      // this thread's max |D1|: NaN if a block holds one; then (rarely) the
+      // NaN-ignoring maximum, which the reference's tile amax takes.  The
+      // reload is warp-wide (tcgen05.ld is .sync.aligned); lanes without a NaN
+      // get their own maximum again.
+      float tmax = max3_nan(am[0], am[1], max3_nan(am[2], am[3], 0.0f));
+      if (__any_sync(0xffffffffu, isnan(tmax))) {
+        tmax = amax_ignore_nan(x0);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
-      if (lane == 0) atomicMax(&sm.amax_bits[grp][l & 1], __float_as_uint(tmax));
+        for (int q = 0; q < 2; ++q) {  // columns 32-63, 16 at a time (x0 stays live)
+          float y[16];
+          tc::ld_32x32b_x16(ta + 32 + 16 * q, y);
+          tc::ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) tmax = fmaxf(tmax, fabsf(y[e]));
+        }
+      }
+      // the warp's maximum in one reduction (non-negative floats order as their bits)
+      const uint32_t wmax = __reduce_max_sync(0xffffffffu, __float_as_uint(tmax));
+      if (lane == 0) atomicMax(&sm.amax_bits[grp][l & 1], wmax);
 #pragma unroll
       for (int b = 0; b < 4; ++b) ws[b] = scale_w(am[b]);
       named_bar(bar_id, 256);

@@ -68,6 +68,43 @@ __device__ __forceinline__ float block_amax3(const float2 (&x)[8 * NB], float (&
   return tmax;
 }
 
+// As block_amax3 without the per-block NaN test: am[blk] = max |x| of block
+// blk, NaN when the block holds one.  The caller folds the block maxima with
+// max3_nan and takes the NaN-ignoring maximum (amax_ignore_nan) only in the
+// rare case that the fold is NaN.
+template <int NB>
+__device__ __forceinline__ void block_amax3_raw(const float2 (&x)[8 * NB], float (&am)[NB]) {
+#pragma unroll
+  for (int blk = 0; blk < NB; ++blk) {
+    const float2* xb = x + 8 * blk;
+    float m0, m1, mb;
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(xb[0].x), "f"(xb[0].y), "f"(xb[1].x));
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m1) : "f"(xb[1].y), "f"(xb[2].x), "f"(xb[2].y));
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(m0), "f"(xb[3].x), "f"(xb[3].y));
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m1) : "f"(m1), "f"(xb[4].x), "f"(xb[4].y));
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(m0), "f"(xb[5].x), "f"(xb[5].y));
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m1) : "f"(m1), "f"(xb[6].x), "f"(xb[6].y));
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(m0) : "f"(m0), "f"(xb[7].x), "f"(xb[7].y));
+    asm("max.NaN.abs.f32 %0, %1, %2, %3;" : "=f"(mb) : "f"(m0), "f"(m1), "f"(0.0f));
+    am[blk] = mb;
+  }
+}
+
+// max of three non-negative-or-NaN values, NaN if any is NaN.
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// max |x| over 16 pairs, NaN ignored (the reference's fmaxf scan); 0 if all are NaN.
+__device__ __forceinline__ float amax_ignore_nan(const float2 (&x)[16]) {
+  float m = 0.0f;
+#pragma unroll
+  for (int p = 0; p < 16; ++p) m = fmaxf(m, fmaxf(fabsf(x[p].x), fabsf(x[p].y)));
+  return m;
+}
+
 // Quantises the NB 16-element blocks of x with the tile's inverse global
 // scale.  am[blk] = max |x| of block blk (NaN when the block holds one).
 // inv_tab[s] = 1 / decode(s) for every scale byte s.  Writes the 8 NB code
