@@ -70,7 +70,7 @@ constexpr uint32_t kOffV = 2 * kStageKQ;             // v of the chunk the prep 
 constexpr uint32_t kOffSB = kOffV + 2 * kBox;        // chain: bf16 state copy S^T [j][i]
 constexpr uint32_t kOffScr = kOffSB + 32768;         // prep: solve scratch, T diag(beta)
 constexpr int kLd = 68;                              // solve scratch row pitch (floats)
-constexpr int kXLd = 16;                             // X^T row pitch (floats)
+constexpr int kXLd = 16;                             // X^T scratch: 64 x 16 floats (6 tiles of 8 x 20 in the solve)
 constexpr int kDLd = 20;                             // diagonal-block inverse row pitch (floats)
 constexpr uint32_t kSizeScr = 2 * 64 * kLd * 4 + 64 * kXLd * 4 + 64 * kDLd * 4;
 constexpr uint32_t kOffHand = kOffScr + kSizeScr;    // prep -> chain, double-buffered
@@ -274,6 +274,35 @@ __device__ __forceinline__ int32_t seq_slot(const PrefillArgs& a, int n, bool re
   return slot;
 }
 
+// x rounded to tf32 (nearest, ties away from zero): a float whose low 13
+// significand bits are zero, so that a tf32 MMA operand holds it exactly.
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+__device__ __forceinline__ void mma_16x8x8_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// d (16 x 8) += a (16 x 8) b (8 x 8) on the tensor cores, operands already
+// rounded to tf32 (tf32_round).  Warp-level fragments (PTX mma.m16n8k8
+// .tf32): lane l, group g = l / 4, t = l % 4, holds a at rows g, g + 8 and
+// columns t, t + 4 (a0 = [g][t], a1 = [g + 8][t], a2 = [g][t + 4],
+// a3 = [g + 8][t + 4]), b at rows t, t + 4 of column g, and d at rows g,
+// g + 8, columns 2t, 2t + 1.
+__device__ __forceinline__ void mma_16x8x8_f(float (&d)[4], float a0, float a1, float a2, float a3, float b0,
+                                             float b1) {
+  mma_16x8x8_tf32(d, __float_as_uint(a0), __float_as_uint(a1), __float_as_uint(a2), __float_as_uint(a3),
+                  __float_as_uint(b0), __float_as_uint(b1));
+}
+
 template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
     gdn_prefill_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tm_q,
@@ -318,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ================================== prep ==================================
     float* const Am = reinterpret_cast<float*>(smem + kOffScr);
     float* const Tt = Am + 64 * kLd;   // T^T: Tt[j * kLd + r] = T[r][j]
-    float* const Xt = Tt + 64 * kLd;   // X^T of the current block row: Xt[j * kXLd + t]
+    float* const Xt = Tt + 64 * kLd;   // per-warp X^T tiles of the block-row solve (8 x 20 floats each)
     float* const Dm = Xt + 64 * kXLd;  // the diagonal blocks of T, row-major: Dm[(16 b + r) * kDLd + c]
     uint8_t* const tpp = smem + kOffScr;  // T diag(beta), bf16 K-major [r][s], over A once A is consumed
     const uint32_t id_kq = tc::idesc_bf16(128, 64);
@@ -472,11 +501,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             vals[4 * c4 + 3] *= d4.w;
           }
         }
-        if (arow) {
+        if (arow) {  // A in tf32, the precision of the solve's products
 #pragma unroll
           for (int c4 = 0; c4 < 8; ++c4)
             *reinterpret_cast<float4*>(Am + r * kLd + sb0 + 4 * c4) =
-                make_float4(vals[4 * c4], vals[4 * c4 + 1], vals[4 * c4 + 2], vals[4 * c4 + 3]);
+                make_float4(tf32_round(vals[4 * c4]), tf32_round(vals[4 * c4 + 1]), tf32_round(vals[4 * c4 + 2]),
+                            tf32_round(vals[4 * c4 + 3]));
         } else {
 #pragma unroll
           for (int c8 = 0; c8 < 4; ++c8)
@@ -511,6 +541,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         float4* tcol = reinterpret_cast<float4*>(Tt + (16 * b + c) * kLd + 16 * b);
   #pragma unroll
+        for (int r = 0; r < 16; ++r) x[r] = tf32_round(x[r]);  // T in tf32, the precision of the solve's products
+  #pragma unroll
         for (int r4 = 0; r4 < 4; ++r4) tcol[r4] = make_float4(x[4 * r4], x[4 * r4 + 1], x[4 * r4 + 2], x[4 * r4 + 3]);
   #pragma unroll
         for (int r = 0; r < 16; ++r) Dm[(16 * b + r) * kDLd + c] = x[r];
@@ -524,43 +556,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       group_sync(kBarPrep);
+      // Block rows 1-3 on warp-level tensor-core MMAs (m16n8k8; A, T and X are
+      // stored rounded to tf32): warp w < 2 ib owns the 8 columns n0 = 8 w of
+      // block row ib and needs no other warp until the row is done.
+      // X = A[block row ib][.] T[.][n0 : n0 + 8] over the K steps where that
+      // column strip of T is nonzero, then T[block row ib][n0 : n0 + 8] =
+      // -D_ib X through an 8 x 16 scratch tile of its own (pitch 20:
+      // conflict-free fragment stores and loads).  The m16n8k8 shape fits these
+      // 16-row products; tcgen05 MMAs start at 64 rows.
+      const int fg = lane >> 2, ft = lane & 3;  // fragment group and thread-in-group
   #pragma unroll
       for (int ib = 1; ib < 4; ++ib) {
-        const int r = tid & 15, jj = tid >> 4;
-        // X = A[block row ib][0 : 16 ib] T[0 : 16 ib][0 : 16 ib]  (column j of T is zero above row 16 m)
-  #pragma unroll
-        for (int m = 0; m < ib; ++m) {
-          const int j = jj + 16 * m;
-          const float4* arow = reinterpret_cast<const float4*>(Am + (16 * ib + r) * kLd);
-          const float4* tcol = reinterpret_cast<const float4*>(Tt + j * kLd);
+        if (warp < 2 * ib) {
+          const int n0 = 8 * warp;
           float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  #pragma unroll
-          for (int k4 = 4 * m; k4 < 4 * ib; ++k4) {
-            const float4 av = arow[k4], tv = tcol[k4];
-            acc[0] = fmaf(av.x, tv.x, acc[0]);
-            acc[1] = fmaf(av.y, tv.y, acc[1]);
-            acc[2] = fmaf(av.z, tv.z, acc[2]);
-            acc[3] = fmaf(av.w, tv.w, acc[3]);
+          for (int k = 16 * (n0 >> 4); k < 16 * ib; k += 8) {
+            const float* ar = Am + (16 * ib + fg) * kLd + k + ft;
+            const float* tr = Tt + (n0 + fg) * kLd + k + ft;
+            mma_16x8x8_f(acc, ar[0], ar[8 * kLd], ar[4], ar[8 * kLd + 4], tr[0], tr[4]);
           }
-          Xt[j * kXLd + r] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-        }
-        group_sync(kBarPrep);
-        // T[block row ib][0 : 16 ib] = -D_ib X
+          float* const xw = Xt + 160 * warp;  // X^T tile: xw[n * 20 + k] = X[k][n0 + n]
+          xw[(2 * ft) * 20 + fg] = tf32_round(acc[0]);
+          xw[(2 * ft + 1) * 20 + fg] = tf32_round(acc[1]);
+          xw[(2 * ft) * 20 + fg + 8] = tf32_round(acc[2]);
+          xw[(2 * ft + 1) * 20 + fg + 8] = tf32_round(acc[3]);
+          __syncwarp();
+          float acc2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   #pragma unroll
-        for (int m = 0; m < ib; ++m) {
-          const int j = jj + 16 * m;
-          const float4* drow = reinterpret_cast<const float4*>(Dm + (16 * ib + r) * kDLd);
-          const float4* xcol = reinterpret_cast<const float4*>(Xt + j * kXLd);
-          float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  #pragma unroll
-          for (int t4 = 0; t4 < 4; ++t4) {
-            const float4 dv = drow[t4], xv = xcol[t4];
-            acc[0] = fmaf(dv.x, xv.x, acc[0]);
-            acc[1] = fmaf(dv.y, xv.y, acc[1]);
-            acc[2] = fmaf(dv.z, xv.z, acc[2]);
-            acc[3] = fmaf(dv.w, xv.w, acc[3]);
+          for (int k2 = 0; k2 < 16; k2 += 8) {
+            const float* dr = Dm + (16 * ib + fg) * kDLd + k2 + ft;
+            const float* xr = xw + fg * 20 + k2 + ft;
+            mma_16x8x8_f(acc2, dr[0], dr[8 * kDLd], dr[4], dr[8 * kDLd + 4], xr[0], xr[4]);
           }
-          Tt[j * kLd + 16 * ib + r] = -((acc[0] + acc[1]) + (acc[2] + acc[3]));
+          Tt[(n0 + 2 * ft) * kLd + 16 * ib + fg] = tf32_round(-acc2[0]);
+          Tt[(n0 + 2 * ft + 1) * kLd + 16 * ib + fg] = tf32_round(-acc2[1]);
+          Tt[(n0 + 2 * ft) * kLd + 16 * ib + fg + 8] = tf32_round(-acc2[2]);
+          Tt[(n0 + 2 * ft + 1) * kLd + 16 * ib + fg + 8] = tf32_round(-acc2[3]);
+          __syncwarp();  // the scratch tile is read before the next block row rewrites it
         }
         group_sync(kBarPrep);
       }
