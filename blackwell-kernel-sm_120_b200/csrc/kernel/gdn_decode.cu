@@ -124,9 +124,9 @@ struct __align__(1024) DecodeSmem {
   float inv_tab[256];
   uint32_t rtab[8];                 // scale_inv_w's reciprocal significands
   uint64_t full[kStages], ready[kStages], empty[kStages];
-  // per group: bar_t D1' in X_g (MMA1' committed), bar_w w formed (D1' read), bar_d D1 in
-  // X_g (MMA1 and the rank-1 update committed), bar_x X_g free (D1 read)
-  uint64_t bar_t[kGroups], bar_w[kGroups], bar_d[kGroups], bar_x[kGroups], bar_fin[2];
+  // per group: bar_t D1' in X_g (MMA1' committed), bar_r D1' read, bar_w w formed, bar_d D1
+  // in X_g (MMA1 and the rank-1 update committed), bar_x X_g free (D1 read)
+  uint64_t bar_t[kGroups], bar_r[kGroups], bar_w[kGroups], bar_d[kGroups], bar_x[kGroups], bar_fin[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -256,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.bar_w[g], 4);   // the group's four output warps
       mbar_init(&sm.bar_d[g], 2);   // the back warp's arrival + its commit
       mbar_init(&sm.bar_x[g], 8);   // the group's eight warps
+      mbar_init(&sm.bar_r[g], 8);   // likewise
       sm.amax_bits[g][0] = sm.amax_bits[g][1] = 0u;
     }
     mbar_init(&sm.bar_fin[0], 1);
@@ -566,18 +567,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int g = n % kGroups;
         if (!wait_bar(&sm.ready[s], (uint32_t)((n / kStages) & 1), abort_flag)) { ok = false; break; }
         if (sm.ring[n & (kRing - 1)].end) break;
-        // MMA1(n) + MMA_r1(n) into X_g once the group has formed w(n)
+        const uint64_t so = s * kStageDesc;
+        const int drop = sm.ring[n & (kRing - 1)].drop;
+        const uint32_t sf = T + kColSF + 8 * (uint32_t)(n & (kSfSlots - 1));
+        const uint32_t d = T + kColX + 128 * (uint32_t)g;
+        // MMA1(n) into X_g once every warp of the group has read D1'(n), which
+        // is early in its phase A: the decode overlaps the dot products
+        if (!wait_bar(&sm.bar_r[g], (uint32_t)((n / kGroups) & 1), abort_flag)) { ok = false; break; }
+        tc::fence_after_sync();
+        if (lane == 0 && !drop) {
+          tc::mma_mxf4nvf4_c<false>(d, d_codes + so, d_ident0, id_mx, sf, t_one);
+          tc::mma_mxf4nvf4_c<true>(d, d_codes + so + 2, d_ident1, id_mx, sf + 4, t_one + 4);
+        }
+        __syncwarp();
+        // MMA_r1(n) once the group has formed w(n)
         if (!wait_bar(&sm.bar_w[g], (uint32_t)((n / kGroups) & 1), abort_flag)) { ok = false; break; }
         tc::fence_after_sync();
         if (lane == 0) {
-          const uint64_t so = s * kStageDesc;
-          const int drop = sm.ring[n & (kRing - 1)].drop;
-          const uint32_t sf = T + kColSF + 8 * (uint32_t)(n & (kSfSlots - 1));
-          const uint32_t d = T + kColX + 128 * (uint32_t)g;
-          if (!drop) {
-            tc::mma_mxf4nvf4_c<false>(d, d_codes + so, d_ident0, id_mx, sf, t_one);
-            tc::mma_mxf4nvf4_c<true>(d, d_codes + so + 2, d_ident1, id_mx, sf + 4, t_one + 4);
-          }
           tc::mma_tf32_ss(d, d_ak + so, d_bw + (uint64_t)g * kBwDesc, id_r1, drop ? 0u : 1u);
           mbar_arrive(&sm.bar_d[g]);  // publishes the ring entry to the group's requantiser phase
           tc::commit_at(b_d0 + 8 * g);
@@ -632,6 +638,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           float2 x[16];
           tc::ld_32x32b_x32(ta + 32 * h2, reinterpret_cast<float*>(x));
           tc::ld_wait();
+          if (h2 == 1) {
+            // D1' is read: the back warp may decode D1 into X_g
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.bar_r[grp]);
+          }
           const float4* kq4 = st.kq4 + 32 * half + 16 * h2;
 #pragma unroll
           for (int p = 0; p < 16; p += 2) {
@@ -642,9 +654,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             sp1 = __ffma2_rn(x[p + 1], make_float2(kb.z, kb.w), sp1);
           }
         }
-        // D1' is read; the barrier below and bar_w order these loads before
-        // the back warp's MMA1, which overwrites X_g
-        tc::fence_before_sync();
         const float2 su = __fadd2_rn(su0, su1), sp = __fadd2_rn(sp0, sp1);
         if (half) sm.red[grp][row] = make_float2(su.x + su.y, sp.x + sp.y);
         named_bar(bar_id, 256);
