@@ -274,13 +274,6 @@ __device__ __forceinline__ int32_t seq_slot(const PrefillArgs& a, int n, bool re
   return slot;
 }
 
-// x rounded to tf32 (nearest, ties away from zero): a float whose low 13
-// significand bits are zero, so that a tf32 MMA operand holds it exactly.
-__device__ __forceinline__ float tf32_round(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
 
 __device__ __forceinline__ void mma_16x8x8_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                 uint32_t b0, uint32_t b1) {
@@ -291,8 +284,9 @@ __device__ __forceinline__ void mma_16x8x8_tf32(float (&d)[4], uint32_t a0, uint
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// d (16 x 8) += a (16 x 8) b (8 x 8) on the tensor cores, operands already
-// rounded to tf32 (tf32_round).  Warp-level fragments (PTX mma.m16n8k8
+// d (16 x 8) += a (16 x 8) b (8 x 8) on the tensor cores with fp32 operands
+// read as tf32 (the MMA uses the top 19 bits of each, i.e. truncates the
+// significand to 10 bits; fp32 accumulate).  Warp-level fragments (PTX mma.m16n8k8
 // .tf32): lane l, group g = l / 4, t = l % 4, holds a at rows g, g + 8 and
 // columns t, t + 4 (a0 = [g][t], a1 = [g + 8][t], a2 = [g][t + 4],
 // a3 = [g + 8][t + 4]), b at rows t, t + 4 of column g, and d at rows g,
@@ -501,12 +495,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             vals[4 * c4 + 3] *= d4.w;
           }
         }
-        if (arow) {  // A in tf32, the precision of the solve's products
+        if (arow) {
 #pragma unroll
           for (int c4 = 0; c4 < 8; ++c4)
             *reinterpret_cast<float4*>(Am + r * kLd + sb0 + 4 * c4) =
-                make_float4(tf32_round(vals[4 * c4]), tf32_round(vals[4 * c4 + 1]), tf32_round(vals[4 * c4 + 2]),
-                            tf32_round(vals[4 * c4 + 3]));
+                make_float4(vals[4 * c4], vals[4 * c4 + 1], vals[4 * c4 + 2], vals[4 * c4 + 3]);
         } else {
 #pragma unroll
           for (int c8 = 0; c8 < 4; ++c8)
@@ -541,8 +534,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         float4* tcol = reinterpret_cast<float4*>(Tt + (16 * b + c) * kLd + 16 * b);
   #pragma unroll
-        for (int r = 0; r < 16; ++r) x[r] = tf32_round(x[r]);  // T in tf32, the precision of the solve's products
-  #pragma unroll
         for (int r4 = 0; r4 < 4; ++r4) tcol[r4] = make_float4(x[4 * r4], x[4 * r4 + 1], x[4 * r4 + 2], x[4 * r4 + 3]);
   #pragma unroll
         for (int r = 0; r < 16; ++r) Dm[(16 * b + r) * kDLd + c] = x[r];
@@ -556,9 +547,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       group_sync(kBarPrep);
-      // Block rows 1-3 on warp-level tensor-core MMAs (m16n8k8; A, T and X are
-      // stored rounded to tf32): warp w < 2 ib owns the 8 columns n0 = 8 w of
-      // block row ib and needs no other warp until the row is done.
+      // Block rows 1-3 on warp-level tensor-core MMAs (m16n8k8, tf32 operands):
+      // warp w < 2 ib owns the 8 columns n0 = 8 w of block row ib and needs no
+      // other warp until the row is done.
       // X = A[block row ib][.] T[.][n0 : n0 + 8] over the K steps where that
       // column strip of T is nonzero, then T[block row ib][n0 : n0 + 8] =
       // -D_ib X through an 8 x 16 scratch tile of its own (pitch 20:
@@ -576,10 +567,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_16x8x8_f(acc, ar[0], ar[8 * kLd], ar[4], ar[8 * kLd + 4], tr[0], tr[4]);
           }
           float* const xw = Xt + 160 * warp;  // X^T tile: xw[n * 20 + k] = X[k][n0 + n]
-          xw[(2 * ft) * 20 + fg] = tf32_round(acc[0]);
-          xw[(2 * ft + 1) * 20 + fg] = tf32_round(acc[1]);
-          xw[(2 * ft) * 20 + fg + 8] = tf32_round(acc[2]);
-          xw[(2 * ft + 1) * 20 + fg + 8] = tf32_round(acc[3]);
+          xw[(2 * ft) * 20 + fg] = acc[0];
+          xw[(2 * ft + 1) * 20 + fg] = acc[1];
+          xw[(2 * ft) * 20 + fg + 8] = acc[2];
+          xw[(2 * ft + 1) * 20 + fg + 8] = acc[3];
           __syncwarp();
           float acc2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   #pragma unroll
@@ -588,10 +579,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float* xr = xw + fg * 20 + k2 + ft;
             mma_16x8x8_f(acc2, dr[0], dr[8 * kDLd], dr[4], dr[8 * kDLd + 4], xr[0], xr[4]);
           }
-          Tt[(n0 + 2 * ft) * kLd + 16 * ib + fg] = tf32_round(-acc2[0]);
-          Tt[(n0 + 2 * ft + 1) * kLd + 16 * ib + fg] = tf32_round(-acc2[1]);
-          Tt[(n0 + 2 * ft) * kLd + 16 * ib + fg + 8] = tf32_round(-acc2[2]);
-          Tt[(n0 + 2 * ft + 1) * kLd + 16 * ib + fg + 8] = tf32_round(-acc2[3]);
+          Tt[(n0 + 2 * ft) * kLd + 16 * ib + fg] = -acc2[0];
+          Tt[(n0 + 2 * ft + 1) * kLd + 16 * ib + fg] = -acc2[1];
+          Tt[(n0 + 2 * ft) * kLd + 16 * ib + fg + 8] = -acc2[2];
+          Tt[(n0 + 2 * ft + 1) * kLd + 16 * ib + fg + 8] = -acc2[3];
           __syncwarp();  // the scratch tile is read before the next block row rewrites it
         }
         group_sync(kBarPrep);
