@@ -143,6 +143,12 @@ struct PrefillArgs {
   float* debug_y;
   uint32_t* status;
   int32_t qk_l2norm;  // q and k scaled to unit L2 norm per token and head in the kernel
+  // fused gating (A_log == nullptr: g and beta are read)
+  const float* A_log;
+  const float* dt_bias;
+  const __nv_bfloat16* gate_a;
+  const __nv_bfloat16* gate_b;
+  int64_t gate_stride;
 };
 
 // The global scale of pool tile pt (slot * HV + head).
@@ -252,8 +258,16 @@ __device__ __forceinline__ void load_gb(const PrefillArgs& a, const Cursor& c, i
   bv = 0.0f;
   if (c.item < a.nitems && r < chunk_len(c)) {
     const int64_t idx = (c.bos + c.chunk * kC + r) * a.HV + c.h;
-    gv = __ldg(a.g + idx);
-    bv = __ldg(a.beta + idx);
+    if (a.A_log) {  // g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) (vLLM's gating)
+      const int64_t gi = (c.bos + c.chunk * kC + r) * a.gate_stride + c.h;
+      const float xa = __bfloat162float(a.gate_a[gi]) + __ldg(a.dt_bias + c.h);
+      const float sp = xa > 20.0f ? xa : log1pf(expf(xa));  // torch.nn.functional.softplus, threshold 20
+      gv = -expf(__ldg(a.A_log + c.h)) * sp;
+      bv = 1.0f / (1.0f + expf(-__bfloat162float(a.gate_b[gi])));
+    } else {
+      gv = __ldg(a.g + idx);
+      bv = __ldg(a.beta + idx);
+    }
   }
 }
 
@@ -967,7 +981,10 @@ extern "C" int gdn_prefill(const gdn_prefill_params* p, cudaStream_t stream) {
   if (p->head_dim != kD) return GDN_ERR_UNSUPPORTED;
   if (p->scale_mode != kScaleRef240 && p->scale_mode != kScaleFn448) return GDN_ERR_UNSUPPORTED;
   if (p->num_seqs == 0 || p->total_tokens == 0) return GDN_OK;
-  if (!p->q || !p->k || !p->v || !p->g || !p->beta || !p->cu_seqlens || !p->out) return GDN_ERR_ARGS;
+  if (!p->q || !p->k || !p->v || (!p->A_log && (!p->g || !p->beta)) || !p->cu_seqlens || !p->out)
+    return GDN_ERR_ARGS;
+  const int64_t gate_stride = p->gate_stride ? p->gate_stride : p->num_v_heads;
+  if (p->A_log && (!p->dt_bias || !p->gate_a || !p->gate_b || gate_stride < p->num_v_heads)) return GDN_ERR_ARGS;
   if (p->slot_idx && (!p->pool_codes || !p->pool_scales || !p->pool_gscale)) return GDN_ERR_ARGS;
   int64_t code_stride = 0, scale_stride = 0, gs_stride = 0;
   if (p->slot_idx && !pool_strides(p->pool_tile_stride, p->pool_codes, p->pool_scales, p->pool_gscale,
@@ -1013,6 +1030,11 @@ extern "C" int gdn_prefill(const gdn_prefill_params* p, cudaStream_t stream) {
   a.status = device_status_ptr();
   if (!a.status) return GDN_ERR_CUDA;
   a.qk_l2norm = p->qk_l2norm;
+  a.A_log = p->A_log;
+  a.dt_bias = p->dt_bias;
+  a.gate_a = p->gate_a;
+  a.gate_b = p->gate_b;
+  a.gate_stride = gate_stride;
   CUtensorMap tq, tk, tv;
   if (!make_row_map(&tq, p->q, p->num_k_heads, p->total_tokens, q_stride) ||
       !make_row_map(&tk, p->k, p->num_k_heads, p->total_tokens, k_stride) ||

@@ -87,6 +87,7 @@ class PrefillParams(ctypes.Structure):
         ("debug_y", _p),
         ("pool_tile_stride", _i64),
         ("qk_l2norm", _i32),
+        ("A_log", _p), ("dt_bias", _p), ("gate_a", _p), ("gate_b", _p), ("gate_stride", _i64),
     ]
 
 

@@ -238,23 +238,45 @@ def decode(q, k, v, g, beta, slot_idx, pool, out=None, q_scale: float = 0.0, deb
 
 
 def prefill(q, k, v, g, beta, cu_seqlens, pool=None, slot_idx=None, has_initial_state=None, out=None,
-            q_scale: float = 0.0, debug_y=None, qk_l2norm: bool = False):
+            q_scale: float = 0.0, debug_y=None, qk_l2norm: bool = False, *, A_log=None, dt_bias=None,
+            gate_a=None, gate_b=None):
     """Chunked gated-delta-rule prefill of packed variable-length sequences.
     q, k: [T, HK, D] bf16; v: [T, HV, D] bf16; g, beta: [T, HV] fp32;
     cu_seqlens: [N + 1] int32 (CUDA).  With `pool` and `slot_idx` ([N] int32),
     sequence n starts from the pool state at slot_idx[n] when
     has_initial_state[n] (bool [N]) is set, from zero otherwise, and its final
     state is written back to that slot.  qk_l2norm scales q and k to unit L2
-    norm per token and head inside the kernel.  Returns out [T, HV, D] bf16."""
+    norm per token and head inside the kernel.  Returns out [T, HV, D] bf16.
+
+    Fused gating (vLLM's, as in decode): with A_log ([HV] fp32), dt_bias ([HV]
+    fp32) and the gate projections gate_a, gate_b ([T, HV] bf16), the kernel
+    computes g = -exp(A_log) softplus(gate_a + dt_bias) and beta =
+    sigmoid(gate_b) per token and head (g and beta may then be None)."""
     T, HK, D = q.shape
     HV = v.shape[1]
     for t, name in ((q, "q"), (k, "k"), (v, "v")):
         if t.dtype != torch.bfloat16 or not t.is_cuda or t.stride(-1) != 1 or t.stride(-2) != D:
             raise ValueError(f"{name} must be CUDA bf16 with contiguous heads")
-    _need(g, torch.float32, "g")
-    _need(beta, torch.float32, "beta")
+    fused = A_log is not None
+    if fused:
+        if dt_bias is None:
+            raise ValueError("dt_bias is required with A_log")
+        _need(A_log, torch.float32, "A_log")
+        _need(dt_bias, torch.float32, "dt_bias")
+        for t, name in ((gate_a, "gate_a"), (gate_b, "gate_b")):
+            if t is None or t.dtype != torch.bfloat16 or not t.is_cuda or t.shape != (T, HV) or t.stride(-1) != 1:
+                raise ValueError(f"{name} must be CUDA bf16 [T, HV] with contiguous heads")
+        if gate_a.stride(0) != gate_b.stride(0) or A_log.shape != (HV,) or dt_bias.shape != (HV,):
+            raise ValueError("gate shapes or strides do not match")
+    else:
+        if g is None or beta is None:
+            raise ValueError("g and beta are required unless the gate inputs (A_log, ...) are given")
+        _need(g, torch.float32, "g")
+        _need(beta, torch.float32, "beta")
+        if g.shape != (T, HV) or beta.shape != (T, HV):
+            raise ValueError("shape mismatch")
     _need(cu_seqlens, torch.int32, "cu_seqlens")
-    if k.shape != (T, HK, D) or v.shape != (T, HV, D) or g.shape != (T, HV) or beta.shape != (T, HV):
+    if k.shape != (T, HK, D) or v.shape != (T, HV, D):
         raise ValueError("shape mismatch")
     N = cu_seqlens.numel() - 1
     if N < 0:
@@ -278,7 +300,10 @@ def prefill(q, k, v, g, beta, cu_seqlens, pool=None, slot_idx=None, has_initial_
     p.total_tokens = T
     p.q, p.k, p.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
     p.q_stride, p.k_stride, p.v_stride = q.stride(0), k.stride(0), v.stride(0)
-    p.g, p.beta, p.cu_seqlens = g.data_ptr(), beta.data_ptr(), cu_seqlens.data_ptr()
+    p.g, p.beta, p.cu_seqlens = _ptr(g), _ptr(beta), cu_seqlens.data_ptr()
+    if fused:
+        p.A_log, p.dt_bias = A_log.data_ptr(), dt_bias.data_ptr()
+        p.gate_a, p.gate_b, p.gate_stride = gate_a.data_ptr(), gate_b.data_ptr(), gate_a.stride(0)
     p.has_initial_state = _ptr(has_initial_state)
     if slot_idx is not None:
         p.num_slots = pool.num_slots

@@ -246,6 +246,16 @@ typedef struct gdn_prefill_params {
   int64_t pool_tile_stride; /* pool layout, as in gdn_decode_params (0: dense arrays) */
   int32_t qk_l2norm;      /* != 0: q and k scaled to unit L2 norm per token and head, x / sqrt(sum x^2 + 1e-6),
                              in fp32 inside the kernel (vLLM's use_qk_l2norm_in_kernel) */
+  /* Optional fused gating, as in gdn_decode_params: with A_log set, g and beta
+   * are computed in the kernel for every token t and value head h from the
+   * gate projections, and the g / beta fields are not read:
+   *   g = -exp(A_log[h]) * softplus(gate_a[t, h] + dt_bias[h]),  beta = sigmoid(gate_b[t, h])
+   * (softplus with threshold 20, as torch.nn.functional.softplus). */
+  const float* A_log;       /* [HV] */
+  const float* dt_bias;     /* [HV] */
+  const gdn_bf16_t* gate_a; /* [T, HV], token stride gate_stride */
+  const gdn_bf16_t* gate_b; /* [T, HV], token stride gate_stride */
+  int64_t gate_stride;      /* elements between tokens; 0 = HV */
 } gdn_prefill_params;
 
 GDN_API int gdn_prefill(const gdn_prefill_params* params, cudaStream_t stream);

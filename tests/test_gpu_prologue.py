@@ -1,8 +1,8 @@
-"""GPU checks of the decode kernel's fused prologue (gdn_decode through the C ABI):
-the gating g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) computed in
-the kernel from the gate projections, and the in-kernel unit-L2 scaling of q
-and k -- vLLM's fused_sigmoid_gating_delta_rule_update(use_qk_l2norm_in_kernel)
-contract.
+"""GPU checks of the fused prologue of the decode and prefill kernels (gdn_decode
+and gdn_prefill through the C ABI): the gating g = -exp(A_log) softplus(a +
+dt_bias), beta = sigmoid(b) computed in the kernel from the gate projections,
+and the in-kernel unit-L2 scaling of q and k -- vLLM's
+fused_sigmoid_gating_delta_rule_update(use_qk_l2norm_in_kernel) contract.
 
 * Gating: the fused step equals the same step fed with g and beta computed by
   torch, up to the last bits of exp / log1p (outputs and states agree to
@@ -116,3 +116,56 @@ def test_fused_prologue_argument_errors(cuda):
         ops.decode(q, k, v, None, None, slot, pool, A_log=A_log, dt_bias=dt_bias, gate_a=a, gate_b=None)
     with pytest.raises(ValueError):
         ops.decode(q, k, v, None, None, slot, pool)  # neither g / beta nor the gate inputs
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_prefill_fused_gating_matches_host_gating(cuda, mode):
+    """The chunked prefill with g and beta computed in the kernel from the gate
+    projections equals the prefill fed with torch's g and beta, up to the last
+    bits of exp / log1p: outputs to bf16 rounding, final states to fp32 rounding."""
+    from gdn_b200 import ops, workloads
+    lengths = [70, 1, 200, 64, 129]
+    T = sum(lengths)
+    x = workloads.token_inputs(T, HK, HV, D, seed=12, device="cuda")
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int32, device="cuda")
+    a, b, A_log, dt_bias = _gates(T, seed=13)
+    g = -torch.exp(A_log) * F.softplus(a.float() + dt_bias)
+    beta = torch.sigmoid(b.float())
+    slots = torch.tensor([4, 0, 2, 6, 1], dtype=torch.int32, device="cuda")
+    has = torch.tensor([True, False, True, True, False], device="cuda")
+    pool1, pool2 = _pool(8, mode), _pool(8, mode)
+    o1 = ops.prefill(x["q"], x["k"], x["v"], g, beta, cu, pool=pool1, slot_idx=slots, has_initial_state=has)
+    o2 = ops.prefill(x["q"], x["k"], x["v"], None, None, cu, pool=pool2, slot_idx=slots, has_initial_state=has,
+                     A_log=A_log, dt_bias=dt_bias, gate_a=a, gate_b=b)
+    torch.cuda.synchronize()
+    assert ops.device_status(clear=True) == 0
+    o1f, o2f = o1.float(), o2.float()
+    assert float((o1f - o2f).abs().max()) <= 1e-2 * float(o1f.abs().max())
+    assert float((o1 == o2).float().mean()) > 0.99
+    s1, s2 = pool1.dequantize(), pool2.dequantize()
+    assert float((s1 - s2).abs().max()) <= 2e-2 * float(s1.abs().max())
+    # the slots no sequence uses are untouched
+    for s in (3, 5, 7):
+        assert torch.equal(pool1.codes[s], pool2.codes[s])
+
+
+def test_prefill_fused_gating_argument_errors(cuda):
+    import ctypes
+    from gdn_b200 import _capi, ops, workloads
+    x = workloads.token_inputs(16, HK, HV, D, seed=1, device="cuda")
+    cu = torch.tensor([0, 16], dtype=torch.int32, device="cuda")
+    a, b, A_log, dt_bias = _gates(16)
+    with pytest.raises(ValueError):
+        ops.prefill(x["q"], x["k"], x["v"], None, None, cu, A_log=A_log, gate_a=a, gate_b=b)  # no dt_bias
+    with pytest.raises(ValueError):
+        ops.prefill(x["q"], x["k"], x["v"], None, None, cu, A_log=A_log, dt_bias=dt_bias, gate_a=a)  # no gate_b
+    # C ABI: A_log without gate_b is an argument error
+    p = _capi.PrefillParams()
+    p.num_seqs, p.num_k_heads, p.num_v_heads, p.head_dim = 1, HK, HV, D
+    p.total_tokens = 16
+    p.q, p.k, p.v = x["q"].data_ptr(), x["k"].data_ptr(), x["v"].data_ptr()
+    p.cu_seqlens = cu.data_ptr()
+    out = torch.empty((16, HV, D), dtype=torch.bfloat16, device="cuda")
+    p.out = out.data_ptr()
+    p.A_log, p.dt_bias, p.gate_a = A_log.data_ptr(), dt_bias.data_ptr(), a.data_ptr()
+    assert _capi.lib.gdn_prefill(ctypes.byref(p), None) == _capi.GDN_ERR_ARGS
