@@ -666,11 +666,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float u = su.x + su.y + r.x, p = sp.x + sp.y + r.y;
           const float vj = bf2f(st.v[j]);
           const float wj = m.beta * (vj - c * u);
+          // the stage may be refilled once w is published: the output gate is read first
+          if (kNorm) pend_z = a.gate_z ? bf2f(st.z[j]) : 0.0f;
+          // the rank-1 operand first (the back warp's MMA waits for it), the output after
+          const float wc = wj * m.inv_c;
+          const float hi = __uint_as_float(__float_as_uint(wc) & 0xFFFFE000u);
+          *reinterpret_cast<float*>(bw + kf32(j, 0, 256)) = hi;
+          *reinterpret_cast<float*>(bw + kf32(j, 1, 256)) = wc - hi;
+          tc::fence_smem_to_async();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.bar_w[grp]);
           const float o = a.q_scale * fmaf(m.kq, wj, c * p);
           if (kNorm) {
             // gated RMS norm over the head: x = the bf16 output; this warp's sum of x^2 now
             pend_x = __bfloat162float(__float2bfloat16_rn(o));
-            pend_z = a.gate_z ? bf2f(st.z[j]) : 0.0f;
             float sq = pend_x * pend_x;
 #pragma unroll
             for (int s5 = 16; s5 > 0; s5 >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, s5);
@@ -681,13 +690,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               reinterpret_cast<uint32_t*>(a.out + ((int64_t)m.b * a.HV + m.h) * kD)[j >> 1] =
                   pack_bf16x2(o, o1);  // one paired conversion (faster than two single ones)
           }
-          const float wc = wj * m.inv_c;
-          const float hi = __uint_as_float(__float_as_uint(wc) & 0xFFFFE000u);
-          *reinterpret_cast<float*>(bw + kf32(j, 0, 256)) = hi;
-          *reinterpret_cast<float*>(bw + kf32(j, 1, 256)) = wc - hi;
-          tc::fence_smem_to_async();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.bar_w[grp]);
         }
       }
       // ---------------------------- phase B: requantise D1 ----------------------------
