@@ -455,6 +455,7 @@ PREFILL_FLOP_PER_TOKEN = 5.86e6      # 32 heads x ~11.7 MFLOP per 64-token chunk
 PREFILL_BYTES_PER_TOKEN = 24_832     # q, k, v, o bf16 + g, beta fp32 for 32 value heads
 MIXED_PREFILLS, MIXED_DECODES, MIXED_SLOTS = 48, 512, 2048
 LAYERS, LAYER_BATCH = 36, 1024
+HIDDEN = 2048  # model width the out-projection maps the 32 x 128 value features to (--tail)
 
 
 def _peaks() -> dict:
@@ -645,7 +646,13 @@ def run_layers(args, dist, rank, world, local) -> dict | None:
     """Config 4: 36 GDN layers, batch 1024 decode, value heads sharded over the
     ranks (TP = world: 32/world value and 16/world key heads per GPU), one
     NVFP4 pool of 1024 slots per layer with a seeded random slot map.  Total
-    work is fixed as the rank count grows (strong scaling)."""
+    work is fixed as the rank count grows (strong scaling).
+
+    With --tail every layer runs on to its output (gdn_b200.layer_tail): the
+    decode with vLLM's gated RMS norm fused, the row-parallel out-projection
+    [1024, HV/n * 128] x [HV/n * 128, 2048] (cuBLAS, bf16) and the sum
+    all-reduce of the [1024, 2048] bf16 result over the ranks (NCCL).  The
+    line then also reports each part's mean time per layer."""
     import torch
     from gdn_b200 import NVFP4StatePool, ops, workloads
     dev = torch.device("cuda", local)
@@ -667,22 +674,66 @@ def run_layers(args, dist, rank, world, local) -> dict | None:
                                                                      device=dev).items()})
     out = torch.empty((LAYER_BATCH, hv, D), dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.current_stream(dev)
+    tail = args.tail
+    if tail:
+        from gdn_b200 import layer_tail
+        w_shards, zs = [], []
+        gen_w = torch.Generator(device=dev)
+        for layer in range(LAYERS):
+            gen_w.manual_seed(40_000 + layer)  # the same W_out on every rank; each keeps its column block
+            w_full = (torch.randn((HIDDEN, HV * D), generator=gen_w, device=dev) / (HV * D) ** 0.5).to(torch.bfloat16)
+            w_shards.append(layer_tail.shard_out_proj(w_full, HV, HK, D, rank, world))
+            del w_full
+            zs.append(torch.randn((LAYER_BATCH, hv, D), generator=gen, device=dev).to(torch.bfloat16))
+        gen_w.manual_seed(50_000)
+        norm_w = (1.0 + 0.1 * torch.randn(D, generator=gen_w, device=dev)).to(torch.bfloat16)
+        y = torch.empty((LAYER_BATCH, HIDDEN), dtype=torch.bfloat16, device=dev)
+
+    def decode_one(layer):
+        x = inputs[layer]
+        if tail:
+            return ops.decode(x["q"], x["k"], x["v"], x["g"], x["beta"], slots[layer], pools[layer], out=out,
+                              norm_weight=norm_w, gate_z=zs[layer])
+        return ops.decode(x["q"], x["k"], x["v"], x["g"], x["beta"], slots[layer], pools[layer], out=out)
 
     def step(i):
         for layer in range(LAYERS):
-            x = inputs[layer]
-            ops.decode(x["q"], x["k"], x["v"], x["g"], x["beta"], slots[layer], pools[layer], out=out)
+            o = decode_one(layer)
+            if tail:
+                layer_tail.out_projection(o, w_shards[layer], out=y)
 
+    # the K steps replay from one CUDA graph, the tail's all-reduces included (NCCL records its
+    # kernels into the capture; the graph is released before the process group is destroyed)
     total_ms, clocks = _timed(args, dist, stream, step, local, graph_ok=True)
-    # one decode launch per layer, back to back: the mean launch is the step over the layers
+    # without the tail: one decode launch per layer, back to back, so the mean launch is the step over the layers
     launch_ms = total_ms / args.steps / LAYERS
+    parts = None
+    if tail:
+        # each part of a layer alone, every rank taking part (the all-reduce is a collective)
+        launch_ms = _kernel_ms(args, stream, lambda i: decode_one(i % LAYERS), reps=LAYERS)
+        gemm_ms = _kernel_ms(args, stream, lambda i: torch.matmul(out.view(LAYER_BATCH, -1),
+                                                                  w_shards[i % LAYERS].t(), out=y), reps=LAYERS)
+        ar_ms = 0.0
+        if world > 1:
+            _barrier(dist)
+            ar_ms = _kernel_ms(args, stream, lambda i: dist.all_reduce(y), reps=LAYERS)
+        ar_bytes = y.numel() * y.element_size()
+        parts = {"hidden": HIDDEN, "layer_us": round(total_ms / args.steps / LAYERS * 1e3, 2),
+                 "decode_with_norm_us": round(launch_ms * 1e3, 2), "out_proj_gemm_us": round(gemm_ms * 1e3, 2),
+                 "allreduce_us": round(ar_ms * 1e3, 2), "allreduce_bytes": ar_bytes,
+                 "allreduce_busbw_gbs": (round(ar_bytes * 2 * (world - 1) / world / (ar_ms / 1e3) / 1e9, 1)
+                                         if world > 1 else None)}
     if rank != 0:
         return None
     peaks = _peaks()
     gbs = BYTES_PER_TOKEN * (hv / HV) * LAYER_BATCH / (launch_ms / 1e3) / 1e9
-    cfg = {"workload": "layers36_decode_b1024_hk16_hv32_d128_tp", "layers": LAYERS, "batch": LAYER_BATCH,
+    cfg = {"workload": "layers36_decode_b1024_hk16_hv32_d128_tp" + ("_norm_outproj_allreduce" if tail else ""),
+           "layers": LAYERS, "batch": LAYER_BATCH,
            "v_heads_per_gpu": hv, "k_heads_per_gpu": hk, "parallelism": f"tp{world} (value heads sharded)",
            "pool": "per-layer 1024 slots, random slot map"}
+    if tail:
+        cfg["layer_tail"] = (f"fused gated RMS norm, out-projection {HV * D}->{HIDDEN} (cuBLAS bf16) on the "
+                             f"rank's {hv * D} columns, NCCL sum all-reduce of [{LAYER_BATCH}, {HIDDEN}] bf16")
     line = _base_line(args, world, "GDN 36-layer decode tokens/s (batch 1024)",
                       LAYER_BATCH / (total_ms / args.steps / 1e3), total_ms, cfg, scaling="strong")
     line.update({
@@ -690,6 +741,8 @@ def run_layers(args, dist, rank, world, local) -> dict | None:
                      "unit": "GB/s", "frac": round(gbs / peaks.get("hbm_gbs", 6650.0), 4), "traffic": None,
                      "kernel": "gdn_decode_kernel", "mean_launch_us": round(launch_ms * 1e3, 2)},
         "gpu_launches": LAYERS * args.steps, "clocks": clocks})
+    if parts is not None:
+        line["layer_parts"] = parts
     return line
 
 
@@ -733,6 +786,9 @@ def main() -> None:
     ap.add_argument("--workload", choices=["decode", "prefill", "mixed", "layers"], default="decode",
                     help="decode: batch-256 decode step (the headline); prefill: 8 x 8192-token chunked "
                          "prefill; mixed: 48 varlen prefills + 512 decodes; layers: 36-layer TP decode stack")
+    ap.add_argument("--tail", action="store_true",
+                    help="layers: each layer also applies the fused gated RMS norm, the out-projection and its "
+                         "all-reduce over the ranks")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
