@@ -688,6 +688,10 @@ def run_layers(args, dist, rank, world, local) -> dict | None:
         gen_w.manual_seed(50_000)
         norm_w = (1.0 + 0.1 * torch.randn(D, generator=gen_w, device=dev)).to(torch.bfloat16)
         y = torch.empty((LAYER_BATCH, HIDDEN), dtype=torch.bfloat16, device=dev)
+    peer = None
+    if tail and args.allreduce == "peer" and world > 1:
+        from gdn_b200.peer_allreduce import PeerAllReduce
+        peer = PeerAllReduce(LAYER_BATCH * HIDDEN * 2, device=dev)
 
     def decode_one(layer):
         x = inputs[layer]
@@ -700,7 +704,7 @@ def run_layers(args, dist, rank, world, local) -> dict | None:
         for layer in range(LAYERS):
             o = decode_one(layer)
             if tail:
-                layer_tail.out_projection(o, w_shards[layer], out=y)
+                layer_tail.out_projection(o, w_shards[layer], out=y, allreduce=peer)
 
     # the K steps replay from one CUDA graph, the tail's all-reduces included (NCCL records its
     # kernels into the capture; the graph is released before the process group is destroyed)
@@ -716,13 +720,17 @@ def run_layers(args, dist, rank, world, local) -> dict | None:
         ar_ms = 0.0
         if world > 1:
             _barrier(dist)
-            ar_ms = _kernel_ms(args, stream, lambda i: dist.all_reduce(y), reps=LAYERS)
+            ar_ms = _kernel_ms(args, stream, (lambda i: peer(y, out=y)) if peer is not None else
+                               (lambda i: dist.all_reduce(y)), reps=LAYERS)
         ar_bytes = y.numel() * y.element_size()
         parts = {"hidden": HIDDEN, "layer_us": round(total_ms / args.steps / LAYERS * 1e3, 2),
                  "decode_with_norm_us": round(launch_ms * 1e3, 2), "out_proj_gemm_us": round(gemm_ms * 1e3, 2),
                  "allreduce_us": round(ar_ms * 1e3, 2), "allreduce_bytes": ar_bytes,
                  "allreduce_busbw_gbs": (round(ar_bytes * 2 * (world - 1) / world / (ar_ms / 1e3) / 1e9, 1)
-                                         if world > 1 else None)}
+                                         if world > 1 else None),
+                 "allreduce": "peer (one kernel over NVLink peer memory)" if peer is not None else "nccl"}
+    if peer is not None:
+        peer.close()
     if rank != 0:
         return None
     peaks = _peaks()
@@ -733,7 +741,9 @@ def run_layers(args, dist, rank, world, local) -> dict | None:
            "pool": "per-layer 1024 slots, random slot map"}
     if tail:
         cfg["layer_tail"] = (f"fused gated RMS norm, out-projection {HV * D}->{HIDDEN} (cuBLAS bf16) on the "
-                             f"rank's {hv * D} columns, NCCL sum all-reduce of [{LAYER_BATCH}, {HIDDEN}] bf16")
+                             f"rank's {hv * D} columns, "
+                             f"{'peer-memory' if peer is not None else 'NCCL'} sum all-reduce of "
+                             f"[{LAYER_BATCH}, {HIDDEN}] bf16")
     line = _base_line(args, world, "GDN 36-layer decode tokens/s (batch 1024)",
                       LAYER_BATCH / (total_ms / args.steps / 1e3), total_ms, cfg, scaling="strong")
     line.update({
@@ -786,6 +796,8 @@ def main() -> None:
     ap.add_argument("--workload", choices=["decode", "prefill", "mixed", "layers"], default="decode",
                     help="decode: batch-256 decode step (the headline); prefill: 8 x 8192-token chunked "
                          "prefill; mixed: 48 varlen prefills + 512 decodes; layers: 36-layer TP decode stack")
+    ap.add_argument("--allreduce", choices=["nccl", "peer"], default="nccl",
+                    help="layers --tail: NCCL's all-reduce or this library's peer-memory kernel")
     ap.add_argument("--tail", action="store_true",
                     help="layers: each layer also applies the fused gated RMS norm, the out-projection and its "
                          "all-reduce over the ranks")

@@ -40,6 +40,7 @@ NVCC_FLAGS = ARCH + [
 CUDA_SOURCES = [
     CSRC / "runtime" / "status.cu",
     CSRC / "runtime" / "pool.cu",
+    CSRC / "runtime" / "peer_allreduce.cu",
     CSRC / "kernel" / "nvfp4_kernels.cu",
     CSRC / "kernel" / "gdn_decode.cu",
     CSRC / "kernel" / "gdn_prefill.cu",

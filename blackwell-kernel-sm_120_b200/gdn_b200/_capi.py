@@ -40,6 +40,12 @@ EXPORTED_SYMBOLS = (
     "gdn_prefill",
     "gdn_pool_gather",
     "gdn_pool_scatter",
+    "gdn_peer_buffer_bytes",
+    "gdn_peer_buffer_create",
+    "gdn_peer_buffer_open",
+    "gdn_peer_buffer_close",
+    "gdn_peer_buffer_destroy",
+    "gdn_peer_allreduce_bf16",
     "gdn_b200_device_status",
     "gdn_b200_selftest_wait",
     "gdn_b200_selftest_codec",
@@ -91,6 +97,18 @@ class PrefillParams(ctypes.Structure):
     ]
 
 
+class PeerAllReduceParams(ctypes.Structure):
+    """Mirror of gdn_peer_allreduce_params."""
+    _fields_ = [
+        ("bases", _p * 8),
+        ("rank", _i32), ("nranks", _i32),
+        ("capacity_bytes", _i64),
+        ("src", _p), ("dst", _p),
+        ("count", _i64),
+        ("timeout_ns", ctypes.c_uint64),
+    ]
+
+
 def library_path() -> pathlib.Path:
     env = os.environ.get("GDN_B200_LIB")
     return pathlib.Path(env) if env else LIB_DIR / "libgdn_b200.so"
@@ -116,6 +134,12 @@ def _load() -> ctypes.CDLL:
         "gdn_prefill": (ctypes.c_int, [ctypes.POINTER(PrefillParams), _p]),
         "gdn_pool_gather": (ctypes.c_int, [_p, _p, _p, _i64, _i32, _i32, _p, _i32, _p, _p, _p, _p]),
         "gdn_pool_scatter": (ctypes.c_int, [_p, _p, _p, _i64, _i32, _i32, _p, _i32, _p, _p, _p, _p]),
+        "gdn_peer_buffer_bytes": (ctypes.c_int, [_i64, ctypes.POINTER(_i64)]),
+        "gdn_peer_buffer_create": (ctypes.c_int, [_i64, ctypes.POINTER(_p), _p]),
+        "gdn_peer_buffer_open": (ctypes.c_int, [_p, ctypes.POINTER(_p)]),
+        "gdn_peer_buffer_close": (ctypes.c_int, [_p]),
+        "gdn_peer_buffer_destroy": (ctypes.c_int, [_p]),
+        "gdn_peer_allreduce_bf16": (ctypes.c_int, [ctypes.POINTER(PeerAllReduceParams), _p]),
         "gdn_b200_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, _p]),
         "gdn_b200_selftest_wait": (ctypes.c_int, [ctypes.c_uint32, _p, _p]),
         "gdn_b200_selftest_codec": (ctypes.c_int, [_i32, ctypes.c_uint32, _i64, _i32, _p, _p]),

@@ -11,7 +11,9 @@ same projection (src/ops/qwen35_gdn_patch.py:118-121).
 
 The GEMM is a plain library GEMM (cuBLAS through torch.matmul, bf16 in, fp32
 accumulation); the all-reduce is NCCL's over NVLink / NVSwitch (in-switch
-reduction when NCCL selects NVLS).  At the decode shapes of this layer the
+reduction when NCCL selects NVLS) or, with `allreduce=` a
+gdn_b200.peer_allreduce.PeerAllReduce, this library's one-kernel all-reduce
+over peer memory.  At the decode shapes of this layer the
 all-reduce dominates: batch 1024 x hidden 2048 bf16 is 4 MiB per rank, several
 microseconds over NVLink, against ~1.5 microseconds of tensor-core work for
 the GEMM at TP 8 -- so a fused GEMM + reduce kernel could hide little more than
@@ -48,13 +50,15 @@ def _group_size(group) -> int:
 
 
 def out_projection(o: torch.Tensor, w_shard: torch.Tensor, out: torch.Tensor | None = None,
-                   group=None) -> torch.Tensor:
+                   group=None, allreduce=None) -> torch.Tensor:
     """y = sum over the ranks of group of o.reshape(B, -1) @ w_shard^T.
 
     o: [B, HV/n, D] (or [B, HV/n * D]) this rank's attention output; w_shard:
     [hidden, HV/n * D] from shard_out_proj, same dtype.  Returns (or fills) out
     [B, hidden].  Every rank of the group must call it with the same B and
-    hidden (it issues one all-reduce when the group has more than one rank).
+    hidden (it issues one all-reduce when the group has more than one rank):
+    NCCL's, or the callable `allreduce` (a PeerAllReduce over the same ranks),
+    which sums in place.
     """
     B = o.shape[0]
     o2 = o.reshape(B, -1)
@@ -67,7 +71,9 @@ def out_projection(o: torch.Tensor, w_shard: torch.Tensor, out: torch.Tensor | N
     elif out.shape != (B, w_shard.shape[0]) or out.dtype != o2.dtype or not out.is_contiguous():
         raise ValueError("out must be a contiguous [B, hidden] tensor of o's dtype")
     torch.matmul(o2, w_shard.t(), out=out)
-    if _group_size(group) > 1:
+    if allreduce is not None:
+        allreduce(out, out=out)
+    elif _group_size(group) > 1:
         import torch.distributed as dist
         dist.all_reduce(out, op=dist.ReduceOp.SUM, group=group)
     return out
@@ -75,7 +81,7 @@ def out_projection(o: torch.Tensor, w_shard: torch.Tensor, out: torch.Tensor | N
 
 def decode_layer(q, k, v, g, beta, slot_idx, pool, w_shard: torch.Tensor, norm_weight: torch.Tensor,
                  gate_z: torch.Tensor | None = None, *, out: torch.Tensor | None = None,
-                 attn_out: torch.Tensor | None = None, group=None, norm_eps: float = 1e-6,
+                 attn_out: torch.Tensor | None = None, group=None, allreduce=None, norm_eps: float = 1e-6,
                  norm_activation: str = "silu", **decode_kwargs) -> torch.Tensor:
     """One decode step of a tensor-parallel GDN layer from its projections to
     its output: the fused recurrent update with vLLM's gated RMS norm
@@ -85,4 +91,4 @@ def decode_layer(q, k, v, g, beta, slot_idx, pool, w_shard: torch.Tensor, norm_w
     given, receives the normed attention output [B, HV/n, D]."""
     o = ops.decode(q, k, v, g, beta, slot_idx, pool, out=attn_out, norm_weight=norm_weight, gate_z=gate_z,
                    norm_eps=norm_eps, norm_activation=norm_activation, **decode_kwargs)
-    return out_projection(o, w_shard, out=out, group=group)
+    return out_projection(o, w_shard, out=out, group=group, allreduce=allreduce)

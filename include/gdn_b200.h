@@ -5,8 +5,9 @@
  * Conventions
  *   - Plain C types only: device pointers, sizes, a cudaStream_t.  Every call
  *     is stream-ordered and non-blocking: no allocation, no host
- *     synchronisation, no host round trip (gdn_b200_device_status is the one
- *     exception and says so).  The caller owns every buffer.
+ *     synchronisation, no host round trip (gdn_b200_device_status and the
+ *     set-up calls of the peer all-reduce are the exceptions and say so).
+ *     The caller owns every buffer.
  *   - Calls are stateless and safe from any host thread; ordering is per
  *     stream.  The library's only host state is set up once per device under
  *     a lock (the device status word's address, the SM count, the kernels'
@@ -276,6 +277,47 @@ GDN_API int gdn_pool_scatter(const uint8_t* dense_codes, const uint8_t* dense_sc
                      const float* dense_gscale, int64_t num_slots, int32_t num_v_heads,
                      int32_t head_dim, const int32_t* slot_idx, int32_t n, uint8_t* pool_codes,
                      uint8_t* pool_scales, float* pool_gscale, cudaStream_t stream);
+
+/* ---- the out-projection's all-reduce over peer memory ------------------------ */
+/* No counterpart in the reference, whose layer ends in a single-GPU out-projection
+ * (src/ops/qwen35_gdn_patch.py:118-121).  Under tensor parallelism every rank holds
+ * a partial [B, hidden] bf16 product and the layer output is their sum: one
+ * process per GPU, every rank's peer buffer mapped into every other rank. */
+
+/* Bytes of one rank's peer buffer for summands of up to capacity_bytes
+ * (a multiple of 16): 2 * capacity_bytes plus 16 KiB of flags. */
+GDN_API int gdn_peer_buffer_bytes(int64_t capacity_bytes, int64_t* total_bytes);
+
+/* Set-up, once per rank (allocates with cudaMalloc, zeroes and synchronises
+ * the current device): this rank's peer buffer and its CUDA IPC handle
+ * (64 bytes, cudaIpcMemHandle_t) to send to the other ranks. */
+GDN_API int gdn_peer_buffer_create(int64_t capacity_bytes, void** base, void* ipc_handle);
+/* Set-up: maps another rank's peer buffer from its IPC handle. */
+GDN_API int gdn_peer_buffer_open(const void* ipc_handle, void** base);
+/* Tear-down: unmaps another rank's buffer / frees this rank's.  Call them only
+ * when no rank has an all-reduce in flight. */
+GDN_API int gdn_peer_buffer_close(void* base);
+GDN_API int gdn_peer_buffer_destroy(void* base);
+
+typedef struct gdn_peer_allreduce_params {
+  void* bases[8];          /* every rank's peer buffer as mapped in this process (bases[rank]: its own) */
+  int32_t rank, nranks;    /* 1 <= nranks <= 8 */
+  int64_t capacity_bytes;  /* as passed to gdn_peer_buffer_create, the same on every rank */
+  const gdn_bf16_t* src;   /* this rank's summand [count], 16-byte aligned */
+  gdn_bf16_t* dst;         /* the sum [count] (may equal src), 16-byte aligned */
+  int64_t count;           /* multiple of 8 * nranks, 2 * count <= capacity_bytes */
+  uint64_t timeout_ns;     /* bound on each wait for the other ranks (0: 2 s) */
+} gdn_peer_allreduce_params;
+
+/* dst = the sum over the ranks of their src (fp32 sum in rank order, one
+ * rounding to bf16; every rank gets the same bytes).  Every rank must make the
+ * same sequence of calls with the same count; the kernel of one call waits for
+ * the other ranks' kernels of that call (bounded: a wait that runs out sets
+ * GDN_STATUS_WAIT_TIMEOUT and the kernel ends early, after which the buffers
+ * must be re-created).  Calls of one rank must not overlap on the GPU.  The
+ * kernel keeps its own call count in the buffer, so a call captured in a CUDA
+ * graph may be replayed.  Stream-ordered. */
+GDN_API int gdn_peer_allreduce_bf16(const gdn_peer_allreduce_params* params, cudaStream_t stream);
 
 /* ---- library ----------------------------------------------------------------- */
 

@@ -81,7 +81,8 @@ def test_error_strings_and_version():
 
 
 @pytest.mark.parametrize("struct_name,py_name", [("gdn_decode_params", "DecodeParams"),
-                                                 ("gdn_prefill_params", "PrefillParams")])
+                                                 ("gdn_prefill_params", "PrefillParams"),
+                                                 ("gdn_peer_allreduce_params", "PeerAllReduceParams")])
 def test_ctypes_mirrors_match_the_c_layout(tmp_path, struct_name, py_name):
     """The ctypes parameter blocks have the C header's size and field offsets
     (a C program built here with gcc prints them)."""
